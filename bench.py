@@ -1,0 +1,509 @@
+#!/usr/bin/env python
+"""Benchmark of the Whisper attention hot path on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+One step = one pass of encoder self-attention over this rank's share of the
+long-form workload (c4: 64 segments x 20 heads x 1500 frames x 64, bf16,
+scale 1/8; segments split contiguously over the N ranks, no collective on
+the data path).  `value` is whole-job TFLOP/s (4*B*H*N^2*d over the max
+over ranks of the CUDA-event time of K steps).  Extra keys: the roofline of
+the tensor-core kernel, the reference CPU kernel's rate on this host
+(cpu_baseline), an end-to-end number through the host-buffer C-ABI entry
+(e2e: host->device copies, kernels, device->host copies into one shared
+host output), decode-attention HBM GB/s (c3), and SM clocks sampled during
+the timed region.
+
+`--impl reference` times the reference's CPU kernel (the C++ restatement in
+oracle/, all host threads) on a bounded sample of the same workload.
+"""
+
+from __future__ import annotations
+
+import argparse
+import datetime
+import json
+import math
+import os
+import statistics
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "Whisper attn TFLOP/s & decode-attn HBM GB/s per B200; segments/s at 1–8 GPU"
+L2_BYTES = 126 * 2**20
+
+
+def load_peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(p) as f:
+            d = json.load(f)
+        return {"hbm_gbs": float(d["hbm_gbs"]), "bf16_tflops": float(d["bf16_tflops"]),
+                "bf16_tflops_sustained": float(d.get("bf16_tflops_sustained", d["bf16_tflops"])),
+                "source": "measured"}
+    except Exception:
+        return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0,
+                "source": "fallback"}
+
+
+def load_traffic():
+    p = os.path.join(ROOT, "profiles", "traffic.json")
+    try:
+        with open(p) as f:
+            return json.load(f)
+    except Exception:
+        return {}
+
+
+# ----------------------------------------------------------------- clocks
+class ClockSampler:
+    """SM clock and clock-event reasons via NVML every ~5 ms while running."""
+
+    REASONS = {0x4: "sw_power_cap", 0x8: "hw_slowdown", 0x20: "sw_thermal_slowdown",
+               0x40: "hw_thermal_slowdown", 0x80: "hw_power_brake_slowdown",
+               0x2: "applications_clocks_setting", 0x10: "sync_boost"}
+
+    def __init__(self, device_index: int):
+        self.ok = False
+        self.samples = []
+        self.reasons = 0
+        self.max_mhz = None
+        try:
+            import pynvml
+            import torch
+            pynvml.nvmlInit()
+            idx = torch.cuda._get_nvml_device_index(device_index)
+            self.h = pynvml.nvmlDeviceGetHandleByIndex(idx)
+            self.nv = pynvml
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self.h, pynvml.NVML_CLOCK_SM)
+            self.ok = True
+        except Exception:
+            pass
+        self._stop = threading.Event()
+        self._t = None
+
+    def _read(self):
+        nv = self.nv
+        mhz = nv.nvmlDeviceGetClockInfo(self.h, nv.NVML_CLOCK_SM)
+        try:
+            r = nv.nvmlDeviceGetCurrentClocksEventReasons(self.h)
+        except Exception:
+            r = nv.nvmlDeviceGetCurrentClocksThrottleReasons(self.h)
+        self.samples.append(mhz)
+        self.reasons |= int(r)
+
+    def _loop(self):
+        while not self._stop.is_set():
+            try:
+                self._read()
+            except Exception:
+                pass
+            time.sleep(0.005)
+
+    def start(self):
+        if self.ok:
+            self._t = threading.Thread(target=self._loop, daemon=True)
+            self._t.start()
+
+    def stop(self):
+        if self.ok and self._t:
+            self._stop.set()
+            self._t.join()
+            try:
+                self._read()
+            except Exception:
+                pass
+
+    def summary(self):
+        if not self.ok or not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": ["unavailable"]}
+        names = [n for b, n in self.REASONS.items() if self.reasons & b]
+        return {"sm_mhz": statistics.median(self.samples), "sm_max_mhz": self.max_mhz,
+                "reasons": names, "samples": len(self.samples)}
+
+
+# ----------------------------------------------------------------- distributed
+class Dist:
+    def __init__(self):
+        self.world = int(os.environ.get("WORLD_SIZE", "1"))
+        self.rank = int(os.environ.get("RANK", "0"))
+        self.local = int(os.environ.get("LOCAL_RANK", "0"))
+        self.pg = False
+
+    def init(self):
+        import torch
+        torch.cuda.set_device(self.local)
+        if self.world > 1:
+            import torch.distributed as dist
+            dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=180),
+                                    device_id=torch.device("cuda", self.local))
+            self.pg = True
+
+    def barrier(self):
+        if self.pg:
+            import torch.distributed as dist
+            dist.barrier(device_ids=[self.local])
+
+    def max(self, x: float) -> float:
+        if not self.pg:
+            return x
+        import torch
+        import torch.distributed as dist
+        t = torch.tensor([x], dtype=torch.float64, device=f"cuda:{self.local}")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    def sum(self, x: float) -> float:
+        if not self.pg:
+            return x
+        import torch
+        import torch.distributed as dist
+        t = torch.tensor([x], dtype=torch.float64, device=f"cuda:{self.local}")
+        dist.all_reduce(t, op=dist.ReduceOp.SUM)
+        return float(t.item())
+
+    def gather_objects(self, obj):
+        if not self.pg:
+            return [obj]
+        import torch.distributed as dist
+        out = [None] * self.world
+        dist.all_gather_object(out, obj)
+        return out
+
+    def close(self):
+        if self.pg:
+            import torch.distributed as dist
+            dist.destroy_process_group()
+
+
+def timed(dist, steps, fn):
+    """Barrier + sync, K steps between CUDA events, sync + barrier; max over ranks (s)."""
+    import torch
+    dist.barrier()
+    torch.cuda.synchronize()
+    a = torch.cuda.Event(enable_timing=True)
+    b = torch.cuda.Event(enable_timing=True)
+    a.record()
+    for k in range(steps):
+        fn(k)
+    b.record()
+    torch.cuda.synchronize()
+    dist.barrier()
+    local = a.elapsed_time(b) / 1e3
+    return dist.max(local), local
+
+
+# ----------------------------------------------------------------- CPU baseline
+def cpu_encoder_rate(cfg, budget_s: float, seed: int = 0, max_segments: int | None = None):
+    """The reference CPU kernel (oracle restatement, AVX2, all host threads)
+    on `n` segments of the workload, repeated for about `budget_s` seconds.
+    Returns (TFLOP/s, threads, sample description, seconds per run)."""
+    import numpy as np
+    import torch
+
+    from ffai_b200 import workloads
+    from oracle import oracle
+    oracle.build()
+    threads = os.cpu_count() or 1
+    nseg = max(1, min(cfg.segments, math.ceil(threads / cfg.heads)))
+    if max_segments:
+        nseg = min(nseg, max_segments)
+    q, k, v = workloads.encoder_inputs(cfg, seed=seed, segments=nseg)
+    U = nseg * cfg.heads
+    qn = (q.float().numpy() * np.float32(workloads.SCALE)).reshape(U, cfg.seq, 64)
+    ktn = np.ascontiguousarray(np.swapaxes(k.float().numpy().reshape(U, cfg.seq, 64), 1, 2))
+    vn = np.ascontiguousarray(v.float().numpy().reshape(U, cfg.seq, 64))
+    flops = 4.0 * U * cfg.seq * cfg.seq * 64
+    t0 = time.perf_counter()
+    oracle.flash_units(qn, ktn, vn, threads=threads)
+    t_run = time.perf_counter() - t0
+    runs = max(1, int(budget_s / max(t_run, 1e-6)))
+    t0 = time.perf_counter()
+    for _ in range(runs):
+        oracle.flash_units(qn, ktn, vn, threads=threads)
+    dt = time.perf_counter() - t0
+    sample = (f"{nseg} segment(s) x {cfg.heads} heads x {cfg.seq}^2 of {cfg.name} "
+              f"(bf16-rounded, widened to f32), {runs} run(s), {dt:.1f} s")
+    return flops * runs / dt / 1e12, threads, sample, dt / runs, (qn, ktn, vn, flops, threads)
+
+
+def run_reference(args, dist):
+    """`--impl reference`: the reference's CPU kernel, timed on the host cores."""
+    from ffai_b200 import workloads
+    from oracle import oracle
+    if dist.rank != 0:
+        return
+    cfg = workloads.C4
+    per_step_budget = min(10.0, 150.0 / max(1, args.steps + args.warmup))
+    rate, threads, sample, t_run, data = cpu_encoder_rate(cfg, budget_s=1.0)
+    qn, ktn, vn, flops, threads = data
+    runs = max(1, int(per_step_budget / max(t_run, 1e-6)))
+    for _ in range(args.warmup):
+        oracle.flash_units(qn, ktn, vn, threads=threads)
+    times = []
+    for _ in range(args.steps):
+        t0 = time.perf_counter()
+        for _ in range(runs):
+            oracle.flash_units(qn, ktn, vn, threads=threads)
+        times.append(time.perf_counter() - t0)
+    total = sum(times)
+    value = flops * runs * args.steps / total / 1e12
+    nseg = qn.shape[0] // cfg.heads
+    sample = (f"each step: {runs} run(s) of {nseg} segment(s) x {cfg.heads} heads x {cfg.seq}^2 "
+              f"of {cfg.name}, f32 on bf16-rounded inputs")
+    line = {
+        "impl": "reference", "metric": METRIC, "value": round(value, 4), "unit": "TFLOP/s",
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(total / args.steps * 1e3, 3), "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": cfg.name, "segments": cfg.segments, "heads": cfg.heads,
+                   "seq_len": cfg.seq, "head_dim": 64, "scale": workloads.SCALE,
+                   "implementation": "C++ AVX2 restatement of flash_attn.rs (oracle/), "
+                                     "the Rust reference has no toolchain here"},
+        "cpu_baseline": {"value": round(value, 4), "unit": "TFLOP/s", "cores": threads,
+                         "kind": "port", "sample": sample},
+        "e2e": {"value": round(value, 4), "unit": "TFLOP/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+# ----------------------------------------------------------------- decode (c3)
+def bench_decode(steps: int):
+    """Decode attention HBM GB/s on the c3 shapes over distinct per-layer caches
+    (more bytes than L2 per pass), plain launches and one CUDA graph."""
+    import torch
+
+    from ffai_b200 import attention, workloads
+    dev = torch.device("cuda", torch.cuda.current_device())
+    res = {}
+    for name, keys, layers in (("cross_1500", workloads.C3_CROSS_KEYS, 12), ("self_448", 448, 24)):
+        caches = [workloads.decode_inputs(keys, seed=100 + l, device=dev) for l in range(layers)]
+        outs = [torch.empty(5, 12, 1, 64, device=dev) for _ in range(layers)]
+        rows = workloads.C3_BEAMS * workloads.C3_HEADS
+        bytes_per = rows * (2 * keys * 64 * 2) + rows * 64 * (4 + 4)
+
+        def one_pass():
+            for (q, k, v), o in zip(caches, outs):
+                attention.decode(q, k, v, out=o)
+
+        for _ in range(3):
+            one_pass()
+        torch.cuda.synchronize()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        for _ in range(steps):
+            one_pass()
+        b.record()
+        torch.cuda.synchronize()
+        t_launch = a.elapsed_time(b) / 1e3 / (steps * layers)
+        g = torch.cuda.CUDAGraph()
+        s = torch.cuda.Stream()
+        s.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(s):
+            one_pass()
+            torch.cuda.synchronize()
+            with torch.cuda.graph(g, stream=s):
+                one_pass()
+        torch.cuda.current_stream().wait_stream(s)
+        for _ in range(3):
+            g.replay()
+        torch.cuda.synchronize()
+        a.record()
+        for _ in range(steps):
+            g.replay()
+        b.record()
+        torch.cuda.synchronize()
+        t_graph = a.elapsed_time(b) / 1e3 / (steps * layers)
+        del g
+        res[name] = {"rows": rows, "keys": keys, "layers_per_pass": layers,
+                     "bytes_per_launch": bytes_per,
+                     "us_per_launch": round(t_launch * 1e6, 2),
+                     "gbs": round(bytes_per / t_launch / 1e9, 1),
+                     "us_per_launch_graph": round(t_graph * 1e6, 2),
+                     "gbs_graph": round(bytes_per / t_graph / 1e9, 1)}
+    return res
+
+
+# ----------------------------------------------------------------- our arm
+def run_ours(args, dist):
+    import numpy as np
+    import torch
+
+    from ffai_b200 import attention, partition, workloads
+    dist.init()
+    dev = torch.device("cuda", dist.local)
+    peaks = load_peaks()
+    cfg = workloads.C4
+    lo, hi = partition.contiguous_ranges(cfg.segments, dist.world)[dist.rank]
+    nseg = hi - lo
+    seg_bytes = cfg.heads * cfg.seq * 64 * 2
+    shard_in = 3 * nseg * seg_bytes
+    copies = max(1, math.ceil(2 * L2_BYTES / max(shard_in, 1)))
+    inputs = []
+    for c in range(copies):
+        q, k, v = workloads.encoder_inputs(cfg, seed=0, device=dev, segments=nseg, first_segment=lo)
+        if c:
+            # distinct buffers, same values: only the addresses rotate
+            q, k, v = q.clone(), k.clone(), v.clone()
+        inputs.append((q, k, v, torch.empty_like(q)))
+    torch.cuda.synchronize()
+    flops_rank = 4.0 * nseg * cfg.heads * cfg.seq * cfg.seq * 64
+    flops_job = cfg.flops
+
+    launches = [0]
+
+    def step(i):
+        q, k, v, o = inputs[i % copies]
+        attention.prefill(q, k, v, scale=workloads.SCALE, out=o)
+        launches[0] += 1
+
+    for i in range(max(3, args.warmup)):
+        step(i)
+    attention.sync(dist.local)
+
+    # per-launch CUDA events for the kernel duration (roofline), same stream
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+          for _ in range(args.steps)]
+
+    def step_ev(i):
+        ev[i][0].record()
+        step(i)
+        ev[i][1].record()
+
+    clocks = ClockSampler(dist.local)
+    launches[0] = 0
+    clocks.start()
+    t_max, t_local = timed(dist, args.steps, step_ev)
+    clocks.stop()
+    attention.sync(dist.local)
+    n_launch = dist.sum(launches[0])
+    kern = [a.elapsed_time(b) / 1e3 for a, b in ev]
+    k_avg = sum(kern) / len(kern)
+    value = flops_job * args.steps / t_max / 1e12
+    achieved = flops_rank / k_avg / 1e12
+    traffic = load_traffic().get("prefill_tc_kernel", {})
+    tr = traffic.get("dram_bytes_per_segment")
+    roofline = {"bound": "tensor", "achieved": round(achieved, 2), "peak": peaks["bf16_tflops"],
+                "unit": "TFLOP/s", "frac": round(achieved / peaks["bf16_tflops"], 4),
+                "traffic": (int(tr * nseg) if tr else None),
+                "peak_source": f"{peaks['source']} bf16 burst (cuBLAS)",
+                "kernel": "prefill_tc_kernel", "kernel_ms_avg": round(k_avg * 1e3, 4),
+                "algorithmic_flops_per_launch": flops_rank,
+                "algorithmic_bytes_per_launch": int(4 * nseg * seg_bytes)}
+
+    # --- end to end through the host-buffer C-ABI entry, host gather
+    e2e = None
+    if not args.no_e2e:
+        hq, hk, hv = (inputs[0][j].cpu().pin_memory() for j in range(3))
+        out_bytes = cfg.segments * seg_bytes
+        shared = None
+        if dist.world > 1:
+            run_id = os.environ.get("TORCHELASTIC_RUN_ID", os.environ.get("MASTER_PORT", "x"))
+            name = f"ffai_bench_out_{run_id}"
+            if dist.rank == 0:
+                shared = partition.SharedHostBuffer(name, out_bytes, create=True)
+            dist.barrier()
+            if dist.rank != 0:
+                shared = partition.SharedHostBuffer(name, out_bytes, create=False)
+            pinned = shared.pin()
+            raw = torch.frombuffer(shared.map, dtype=torch.bfloat16, count=out_bytes // 2)
+            host_out = raw.view(cfg.segments, cfg.heads, cfg.seq, 64)[lo:hi]
+        else:
+            pinned = True
+            host_out = torch.empty((nseg, cfg.heads, cfg.seq, 64), dtype=torch.bfloat16,
+                                   pin_memory=True)
+
+        def e2e_step(i):
+            attention.prefill_host(hq, hk, hv, device=dist.local, scale=workloads.SCALE,
+                                   out=host_out)
+
+        for i in range(2):
+            e2e_step(i)
+        e_max, _ = timed(dist, max(1, min(args.steps, 10)), e2e_step)
+        e_steps = max(1, min(args.steps, 10))
+        # checksum of checksums: each rank's slice of the shared output equals
+        # its device result; rank 0 checks the gathered whole.
+        mine = partition.checksum(inputs[0][3].view(torch.int16).cpu().numpy())
+        sums = dist.gather_objects(mine)
+        gather_ok = None
+        if dist.rank == 0:
+            whole = raw if dist.world > 1 else host_out.reshape(-1)
+            gather_ok = partition.checksum(whole.view(torch.int16).numpy()) == (
+                sum(sums) % 2**64)
+        e2e = {"value": round(flops_job * e_steps / e_max / 1e12, 3), "unit": "TFLOP/s",
+               "h2d_bytes_per_step": int(3 * cfg.segments * seg_bytes),
+               "d2h_bytes_per_step": int(out_bytes),
+               "ms_per_step": round(e_max / e_steps * 1e3, 3),
+               "entry": "ffai_attn_prefill_host (host buffers, pinned)",
+               "host_gather": ("shared /dev/shm buffer, pinned" if dist.world > 1 and pinned
+                               else "shared /dev/shm buffer, pageable" if dist.world > 1
+                               else "pinned host buffer"),
+               "gather_checksum_ok": gather_ok}
+        dist.barrier()
+        if shared is not None:
+            del raw, host_out
+            shared.close(unlink=dist.rank == 0)
+
+    decode = None
+    if dist.rank == 0 and not args.no_decode:
+        decode = bench_decode(max(5, min(args.steps, 50)))
+        for v_ in decode.values():
+            v_["frac_of_hbm"] = round(v_["gbs_graph"] / peaks["hbm_gbs"], 4)
+
+    cpu = None
+    if dist.rank == 0 and dist.world == 1 and not args.no_cpu_baseline:
+        rate, threads, sample, _, _ = cpu_encoder_rate(cfg, budget_s=args.cpu_seconds)
+        cpu = {"value": round(rate, 4), "unit": "TFLOP/s", "cores": threads, "kind": "port",
+               "sample": sample}
+
+    if dist.rank == 0:
+        line = {
+            "metric": METRIC, "value": round(value, 2), "unit": "TFLOP/s",
+            "n_gpus": dist.world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(t_max / args.steps * 1e3, 4), "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "config": {"workload": cfg.name, "segments": cfg.segments, "heads": cfg.heads,
+                       "seq_len": cfg.seq, "head_dim": 64, "causal": False,
+                       "scale": workloads.SCALE, "out_dtype": "bf16",
+                       "partition": f"{cfg.segments} segments split contiguously over "
+                                    f"{dist.world} rank(s), no data-path collective",
+                       "l2": f"inputs larger than L2: {copies} rotating cop(ies) of "
+                             f"{shard_in / 2**20:.0f} MB per rank"},
+            "segments_per_s": round(cfg.segments * args.steps / t_max, 1),
+            "roofline": roofline,
+            "cpu_baseline": cpu,
+            "e2e": e2e,
+            "gpu_launches": int(n_launch),
+            "clocks": clocks.summary(),
+            "decode": decode,
+        }
+        print(json.dumps(line), flush=True)
+    dist.barrier()
+    dist.close()
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=int(os.environ.get("WORLD_SIZE", "1")))
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-decode", action="store_true")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    args = ap.parse_args()
+    dist = Dist()
+    if args.impl == "reference":
+        run_reference(args, dist)
+        return
+    run_ours(args, dist)
+
+
+if __name__ == "__main__":
+    main()

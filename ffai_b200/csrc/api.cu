@@ -1,0 +1,847 @@
+// C ABI of libffai_attn.so: argument checking (the reference's "decline"
+// contract), per-device context and workspace, tensor-map encoding, work
+// lists, kernel dispatch, the host-buffer pipeline, and the mirror of the
+// reference's candle custom-op surface (crates/ffai-mercury/src/asr/
+// flash_attn.rs).
+#include <cudaTypedefs.h>
+
+#include <algorithm>
+#include <cstdarg>
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+#include <mutex>
+#include <string>
+#include <vector>
+
+#include "../../include/ffai_attn.h"
+#include "kernels.h"
+
+using namespace ffai;
+
+namespace {
+
+constexpr int kHD = 64;
+constexpr int kMinSeq = 256;  // flash_attn.rs:55, performance floor of the encoder shape
+
+thread_local std::string g_tls_error;
+thread_local int g_tls_status = FFAI_ATTN_OK;
+
+// FFAI_DECODE_MIN_KEYS (knobs.rs:163-168, default 8): the decode floor the
+// reference's `serves` and `attend` share (flash_attn.rs:65-67, :112-128).
+int min_decode_keys() {
+  const char* s = std::getenv("FFAI_DECODE_MIN_KEYS");
+  if (s && *s) {
+    char* end = nullptr;
+    const long v = std::strtol(s, &end, 10);
+    if (end && *end == 0 && v >= 0) return static_cast<int>(v);
+  }
+  return 8;
+}
+
+bool env_on(const char* name) {
+  const char* s = std::getenv(name);
+  return s && (!std::strcmp(s, "1") || !std::strcmp(s, "on") || !std::strcmp(s, "true"));
+}
+
+PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
+std::once_flag g_encode_once;
+
+size_t dtype_size(int dt) { return dt == FFAI_DT_F32 ? 4 : 2; }
+
+}  // namespace
+
+struct ffai_attn_ctx {
+  int device = 0;
+  int num_sms = 148;
+  unsigned* d_err = nullptr;
+  // decode workspace
+  float* d_part = nullptr;
+  size_t part_cap = 0;  // floats
+  unsigned* d_counters = nullptr;
+  size_t counters_cap = 0;
+  // prefill work list and per-sequence arrays
+  int4* d_units = nullptr;
+  size_t units_cap = 0;
+  int* d_seq = nullptr;  // q_start | q_len | k_start | k_len, each seq_cap long
+  size_t seq_cap = 0;
+  std::vector<long long> wl_key;
+  int wl_units = 0;
+  int wl_seqs = 0;
+  // bf16 staging for f32 or K^T operands
+  void* d_stage = nullptr;
+  size_t stage_cap = 0;
+  // host pipeline
+  cudaStream_t s_h2d = nullptr, s_comp = nullptr, s_d2h = nullptr;
+  cudaEvent_t ev_h2d[2] = {}, ev_comp[2] = {}, ev_d2h[2] = {};
+  void* d_pipe = nullptr;
+  size_t pipe_cap = 0;
+  ffai_attn_ctx* pipe_ctx = nullptr;  // inner context used for the pipeline's kernels
+  std::string last_error;
+  int last_status = FFAI_ATTN_OK;
+};
+
+namespace {
+
+int set_error(const ffai_attn_ctx* ctx, int status, const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  std::vsnprintf(buf, sizeof buf, fmt, ap);
+  va_end(ap);
+  if (ctx) {
+    auto* c = const_cast<ffai_attn_ctx*>(ctx);
+    c->last_error = buf;
+    c->last_status = status;
+  }
+  g_tls_error = buf;
+  g_tls_status = status;
+  return status;
+}
+
+int cuda_fail(const ffai_attn_ctx* ctx, cudaError_t e, const char* what) {
+  return set_error(ctx, FFAI_ATTN_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
+}
+
+#define FFAI_CUDA(ctx, call)                                \
+  do {                                                      \
+    cudaError_t e_ = (call);                                \
+    if (e_ != cudaSuccess) return cuda_fail(ctx, e_, #call); \
+  } while (0)
+
+// Makes ctx->device current for the duration of a call and restores the
+// caller's device afterwards.
+struct DeviceGuard {
+  int prev = -1;
+  bool ok = true;
+  explicit DeviceGuard(int dev) {
+    if (cudaGetDevice(&prev) != cudaSuccess) prev = -1;
+    if (prev != dev) ok = cudaSetDevice(dev) == cudaSuccess;
+  }
+  ~DeviceGuard() {
+    int cur = -1;
+    if (prev >= 0 && cudaGetDevice(&cur) == cudaSuccess && cur != prev) cudaSetDevice(prev);
+  }
+};
+
+template <typename T>
+int ensure(ffai_attn_ctx* ctx, T** ptr, size_t* cap, size_t need_elems, bool zero = false) {
+  if (*cap >= need_elems && *ptr) return FFAI_ATTN_OK;
+  if (*ptr) {
+    cudaDeviceSynchronize();  // the old buffer may still be read by queued work
+    cudaFree(*ptr);
+    *ptr = nullptr;
+    *cap = 0;
+  }
+  size_t n = std::max<size_t>(need_elems, 1);
+  n = n + n / 4;  // growth slack
+  cudaError_t e = cudaMalloc(reinterpret_cast<void**>(ptr), n * sizeof(T));
+  if (e != cudaSuccess) {
+    *ptr = nullptr;
+    return set_error(ctx, FFAI_ATTN_ERR_NOMEM, "workspace allocation of %zu bytes failed: %s",
+                     n * sizeof(T), cudaGetErrorString(e));
+  }
+  if (zero) {
+    e = cudaMemset(*ptr, 0, n * sizeof(T));
+    if (e != cudaSuccess) return cuda_fail(ctx, e, "cudaMemset(workspace)");
+  }
+  *cap = n;
+  return FFAI_ATTN_OK;
+}
+
+bool valid_dtype(int dt) { return dt == FFAI_DT_F32 || dt == FFAI_DT_BF16 || dt == FFAI_DT_F16; }
+
+// Shape/dtype gate shared by every entry point.  Returns OK, DECLINED (a
+// well-formed request this library does not serve) or ERR_INVALID, with a
+// message.
+int check_desc(const ffai_attn_ctx* ctx, const ffai_attn_desc* d, int op) {
+  if (!d) return set_error(ctx, FFAI_ATTN_ERR_INVALID, "null descriptor");
+  if (d->head_dim != kHD)
+    return set_error(ctx, FFAI_ATTN_DECLINED, "head_dim %d: only 64 is served", d->head_dim);
+  if (d->heads <= 0) return set_error(ctx, FFAI_ATTN_ERR_INVALID, "heads %d <= 0", d->heads);
+  if (!valid_dtype(d->q_dtype) || !valid_dtype(d->kv_dtype))
+    return set_error(ctx, FFAI_ATTN_ERR_INVALID, "unknown dtype (q %d, kv %d)", d->q_dtype,
+                     d->kv_dtype);
+  if (d->out_dtype != FFAI_DT_F32 && d->out_dtype != FFAI_DT_BF16)
+    return set_error(ctx, FFAI_ATTN_DECLINED, "out_dtype %d: f32 or bf16 only", d->out_dtype);
+  if (!(d->scale > 0.f) || !std::isfinite(d->scale))
+    return set_error(ctx, FFAI_ATTN_ERR_INVALID, "scale must be finite and > 0");
+  if (op == FFAI_OP_VARLEN) {
+    if (d->q_layout != FFAI_LAYOUT_TOKEN_MAJOR || d->k_layout != FFAI_LAYOUT_TOKEN_MAJOR ||
+        d->v_layout != FFAI_LAYOUT_TOKEN_MAJOR || d->out_layout != FFAI_LAYOUT_TOKEN_MAJOR)
+      return set_error(ctx, FFAI_ATTN_DECLINED, "varlen: token-major (T,H,64) layouts only");
+    if (d->q_dtype != d->kv_dtype || d->q_dtype == FFAI_DT_F32)
+      return set_error(ctx, FFAI_ATTN_DECLINED, "varlen: bf16 or f16 q/k/v of one type only");
+    if (d->causal) return set_error(ctx, FFAI_ATTN_DECLINED, "varlen: causal not served");
+    return FFAI_ATTN_OK;
+  }
+  if (d->batch <= 0 || d->q_len <= 0 || d->kv_len <= 0)
+    return set_error(ctx, FFAI_ATTN_ERR_INVALID, "batch %d, q_len %d, kv_len %d must be >= 1",
+                     d->batch, d->q_len, d->kv_len);
+  const int cap = d->kv_capacity > 0 ? d->kv_capacity : d->kv_len;
+  if (cap < d->kv_len)
+    return set_error(ctx, FFAI_ATTN_ERR_INVALID, "kv_capacity %d < kv_len %d", cap, d->kv_len);
+  if (d->q_layout == FFAI_LAYOUT_KT || d->v_layout == FFAI_LAYOUT_KT ||
+      d->out_layout == FFAI_LAYOUT_KT)
+    return set_error(ctx, FFAI_ATTN_ERR_INVALID, "only k may use the KT layout");
+  auto layout_ok = [](int l) { return l >= 0 && l <= 2; };
+  if (!layout_ok(d->q_layout) || !layout_ok(d->k_layout) || !layout_ok(d->v_layout) ||
+      !layout_ok(d->out_layout))
+    return set_error(ctx, FFAI_ATTN_ERR_INVALID, "unknown layout");
+  if (d->causal && (d->q_offset < 0))
+    return set_error(ctx, FFAI_ATTN_ERR_INVALID, "causal q_offset %d < 0", d->q_offset);
+
+  if (op == FFAI_OP_DECODE) {
+    if (d->q_len != 1) return set_error(ctx, FFAI_ATTN_DECLINED, "decode: q_len must be 1");
+    if (d->q_dtype != FFAI_DT_F32 && d->q_dtype != d->kv_dtype)
+      return set_error(ctx, FFAI_ATTN_DECLINED, "decode: q must be f32 or the cache dtype");
+    if (d->k_layout == FFAI_LAYOUT_TOKEN_MAJOR || d->v_layout != FFAI_LAYOUT_HEADS_SPLIT)
+      return set_error(ctx, FFAI_ATTN_DECLINED,
+                       "decode: k must be KT or heads-split, v heads-split");
+    return FFAI_ATTN_OK;
+  }
+  // prefill
+  if (d->q_dtype != d->kv_dtype)
+    return set_error(ctx, FFAI_ATTN_DECLINED, "prefill: q and k/v must share a dtype");
+  const bool checked = (d->flags & FFAI_ATTN_FLAG_CHECKED_F32) != 0;
+  if (checked && d->q_dtype != FFAI_DT_F32)
+    return set_error(ctx, FFAI_ATTN_DECLINED, "checked-f32 mode needs f32 operands");
+  if (d->causal && !checked)
+    return set_error(ctx, FFAI_ATTN_DECLINED,
+                     "causal prefill is served by the checked-f32 kernel only");
+  return FFAI_ATTN_OK;
+}
+
+// Element strides (b, h, row, d) of an operand of `rows` rows per head.
+Strides strides_of(int layout, int H, long long rows) {
+  Strides s{};
+  switch (layout) {
+    case FFAI_LAYOUT_HEADS_SPLIT:
+      s = {H * rows * kHD, rows * kHD, kHD, 1};
+      break;
+    case FFAI_LAYOUT_TOKEN_MAJOR:
+      s = {rows * H * kHD, kHD, static_cast<long long>(H) * kHD, 1};
+      break;
+    case FFAI_LAYOUT_KT:
+      s = {H * rows * kHD, rows * kHD, 1, rows};
+      break;
+  }
+  return s;
+}
+
+void init_encoder() {
+  void* fn = nullptr;
+  cudaDriverEntryPointQueryResult q{};
+  if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q) ==
+          cudaSuccess &&
+      q == cudaDriverEntryPointSuccess)
+    g_encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+}
+
+// 3-d bf16/f16 tensor map over 64-element (128-byte) rows with a box of 128
+// rows and 128-byte swizzle.  token_major: dims {64, H, T}; else {64, rows, B*H}.
+int make_map(ffai_attn_ctx* ctx, CUtensorMap* map, const void* base, bool token_major, int H,
+             long long rows_or_tokens, long long groups) {
+  if (!g_encode) return set_error(ctx, FFAI_ATTN_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
+  if (reinterpret_cast<uintptr_t>(base) % 16 != 0)
+    return set_error(ctx, FFAI_ATTN_ERR_INVALID, "operand base address not 16-byte aligned");
+  cuuint64_t dims[3];
+  cuuint64_t strides[2];
+  cuuint32_t box[3];
+  const cuuint32_t estr[3] = {1, 1, 1};
+  if (token_major) {
+    dims[0] = kHD;
+    dims[1] = static_cast<cuuint64_t>(H);
+    dims[2] = static_cast<cuuint64_t>(rows_or_tokens);
+    strides[0] = kHD * 2;
+    strides[1] = static_cast<cuuint64_t>(H) * kHD * 2;
+    box[0] = kHD;
+    box[1] = 1;
+    box[2] = kTcRows;
+  } else {
+    dims[0] = kHD;
+    dims[1] = static_cast<cuuint64_t>(rows_or_tokens);
+    dims[2] = static_cast<cuuint64_t>(groups);
+    strides[0] = kHD * 2;
+    strides[1] = static_cast<cuuint64_t>(rows_or_tokens) * kHD * 2;
+    box[0] = kHD;
+    box[1] = kTcRows;
+    box[2] = 1;
+  }
+  // The data type only sets the element size here (both are 2 bytes).
+  const CUresult r = g_encode(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base),
+                              dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                              CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return set_error(ctx, FFAI_ATTN_ERR_CUDA, "cuTensorMapEncodeTiled: %d", r);
+  return FFAI_ATTN_OK;
+}
+
+// Build (or reuse) the device work list: per-sequence offsets/lengths and
+// units of up to 256 query rows, longest sequences first.
+int prepare_work(ffai_attn_ctx* ctx, const std::vector<int>& q_start, const std::vector<int>& q_len,
+                 const std::vector<int>& k_start, const std::vector<int>& k_len, int H,
+                 cudaStream_t s) {
+  const int nseq = static_cast<int>(q_len.size());
+  std::vector<long long> key;
+  key.reserve(4 * nseq + 2);
+  key.push_back(H);
+  key.push_back(nseq);
+  for (int i = 0; i < nseq; ++i) {
+    key.push_back(q_start[i]);
+    key.push_back(q_len[i]);
+    key.push_back(k_start[i]);
+    key.push_back(k_len[i]);
+  }
+  if (key == ctx->wl_key && ctx->d_units) return FFAI_ATTN_OK;
+
+  std::vector<int> order(nseq);
+  for (int i = 0; i < nseq; ++i) order[i] = i;
+  // Longest-processing-time first: cost ~ q_len * k_len.  Stable, so equal
+  // sequences keep their natural order (adjacent units share K/V in L2).
+  std::stable_sort(order.begin(), order.end(), [&](int a, int b) {
+    return static_cast<long long>(q_len[a]) * k_len[a] > static_cast<long long>(q_len[b]) * k_len[b];
+  });
+  std::vector<int4> units;
+  for (int si : order) {
+    for (int h = 0; h < H; ++h) {
+      for (int r0 = 0; r0 < q_len[si]; r0 += 2 * kTcRows) {
+        const int left = q_len[si] - r0;
+        units.push_back(make_int4(si, h, r0, left > kTcRows ? 2 : 1));
+      }
+    }
+  }
+  int st = ensure(ctx, &ctx->d_units, &ctx->units_cap, units.size());
+  if (st) return st;
+  st = ensure(ctx, &ctx->d_seq, &ctx->seq_cap, 4 * static_cast<size_t>(nseq));
+  if (st) return st;
+  std::vector<int> seq(4 * static_cast<size_t>(nseq));
+  for (int i = 0; i < nseq; ++i) {
+    seq[i] = q_start[i];
+    seq[nseq + i] = q_len[i];
+    seq[2 * nseq + i] = k_start[i];
+    seq[3 * nseq + i] = k_len[i];
+  }
+  FFAI_CUDA(ctx, cudaMemcpyAsync(ctx->d_units, units.data(), units.size() * sizeof(int4),
+                                 cudaMemcpyHostToDevice, s));
+  FFAI_CUDA(ctx, cudaMemcpyAsync(ctx->d_seq, seq.data(), seq.size() * sizeof(int),
+                                 cudaMemcpyHostToDevice, s));
+  // Pageable sources: the copies are staged before these calls return.
+  ctx->wl_key.swap(key);
+  ctx->wl_units = static_cast<int>(units.size());
+  ctx->wl_seqs = nseq;
+  return FFAI_ATTN_OK;
+}
+
+// One TMA operand: base pointer, layout, and the map geometry (rows per
+// (sequence, head) and head groups for heads-split; tokens for token-major).
+struct Operand {
+  const void* ptr;
+  bool token_major;
+  long long rows;
+  long long groups;
+};
+
+int run_tc(ffai_attn_ctx* ctx, const Operand& q, const Operand& k, const Operand& v, int H,
+           int ab_f16, void* o, int out_bf16, bool out_tm, long long out_rows, float* lse,
+           long long lse_tokens, float scale, cudaStream_t s) {
+  CUtensorMap tq, tk, tv;
+  int st = make_map(ctx, &tq, q.ptr, q.token_major, H, q.rows, q.groups);
+  if (st) return st;
+  st = make_map(ctx, &tk, k.ptr, k.token_major, H, k.rows, k.groups);
+  if (st) return st;
+  st = make_map(ctx, &tv, v.ptr, v.token_major, H, v.rows, v.groups);
+  if (st) return st;
+  TcParams p{};
+  p.units = ctx->d_units;
+  p.num_units = ctx->wl_units;
+  p.q_start = ctx->d_seq;
+  p.q_len = ctx->d_seq + ctx->wl_seqs;
+  p.k_start = ctx->d_seq + 2 * ctx->wl_seqs;
+  p.k_len = ctx->d_seq + 3 * ctx->wl_seqs;
+  p.heads = H;
+  p.q_token_major = q.token_major;
+  p.k_token_major = k.token_major;
+  p.v_token_major = v.token_major;
+  p.out = o;
+  p.out_bf16 = out_bf16;
+  p.out_token_major = out_tm;
+  p.out_rows = out_rows;
+  p.lse = lse;
+  p.lse_tokens = lse_tokens;
+  p.scale_log2 = scale * 1.4426950408889634f;
+  p.err = ctx->d_err;
+  const int grid = std::min(ctx->wl_units, ctx->num_sms);
+  if (grid <= 0) return FFAI_ATTN_OK;
+  FFAI_CUDA(ctx, launch_prefill_tc(tq, tk, tv, p, grid, ab_f16, s));
+  return FFAI_ATTN_OK;
+}
+
+int prefill_impl(ffai_attn_ctx* ctx, const ffai_attn_desc* d, const void* q, const void* k,
+                 const void* v, void* o, float* lse, cudaStream_t s) {
+  const int B = d->batch, H = d->heads, Nq = d->q_len, Nk = d->kv_len;
+  const int cap = d->kv_capacity > 0 ? d->kv_capacity : Nk;
+  const bool out_tm = d->out_layout == FFAI_LAYOUT_TOKEN_MAJOR;
+
+  if (d->flags & FFAI_ATTN_FLAG_CHECKED_F32) {
+    SimtParams p{};
+    p.q = static_cast<const float*>(q);
+    p.k = static_cast<const float*>(k);
+    p.v = static_cast<const float*>(v);
+    p.out = o;
+    p.lse = lse;
+    p.qs = strides_of(d->q_layout, H, Nq);
+    p.ks = strides_of(d->k_layout, H, cap);
+    p.vs = strides_of(d->v_layout, H, cap);
+    p.os = strides_of(d->out_layout, H, Nq);
+    if (out_tm) {
+      p.lse_sb = Nq;
+      p.lse_sh = static_cast<long long>(B) * Nq;
+    } else {
+      p.lse_sb = static_cast<long long>(H) * Nq;
+      p.lse_sh = Nq;
+    }
+    p.B = B;
+    p.H = H;
+    p.Nq = Nq;
+    p.Nk = Nk;
+    p.out_dtype = d->out_dtype;
+    p.causal = d->causal;
+    p.q_offset = d->q_offset;
+    p.scale = d->scale;
+    FFAI_CUDA(ctx, launch_prefill_simt(p, s));
+    return FFAI_ATTN_OK;
+  }
+
+  // Tensor-core path: operands must be 16-bit in heads-split or token-major
+  // layout.  f32 operands are gathered into bf16 staging; K^T (whose row
+  // pitch TMA cannot describe in general) is gathered into heads-split rows
+  // of its own 16-bit type.
+  const bool f32 = d->q_dtype == FFAI_DT_F32;
+  const int dt16 = f32 ? FFAI_DT_BF16 : d->q_dtype;
+  const bool stage_q = f32;
+  const bool stage_k = f32 || d->k_layout == FFAI_LAYOUT_KT;
+  const bool stage_v = f32;
+  const size_t q_elems = static_cast<size_t>(B) * H * Nq * kHD;
+  const size_t kv_elems = static_cast<size_t>(B) * H * Nk * kHD;
+  const size_t stage = (stage_q ? q_elems : 0) + (stage_k ? kv_elems : 0) + (stage_v ? kv_elems : 0);
+  const void *qq = q, *kk = k, *vv = v;
+  bool q_tm = d->q_layout == FFAI_LAYOUT_TOKEN_MAJOR;
+  bool k_tm = d->k_layout == FFAI_LAYOUT_TOKEN_MAJOR;
+  bool v_tm = d->v_layout == FFAI_LAYOUT_TOKEN_MAJOR;
+  int kcap = cap, vcap = cap;
+  if (stage) {
+    int st = ensure(ctx, reinterpret_cast<uint16_t**>(&ctx->d_stage), &ctx->stage_cap, stage);
+    if (st) return st;
+    uint16_t* base = static_cast<uint16_t*>(ctx->d_stage);
+    if (stage_q) {
+      FFAI_CUDA(ctx, launch_to_16bit_heads_split(q, d->q_dtype, strides_of(d->q_layout, H, Nq), B,
+                                                 H, Nq, base, dt16 == FFAI_DT_F16, s));
+      qq = base;
+      q_tm = false;
+      base += q_elems;
+    }
+    if (stage_k) {
+      FFAI_CUDA(ctx, launch_to_16bit_heads_split(k, d->kv_dtype, strides_of(d->k_layout, H, cap), B,
+                                                 H, Nk, base, dt16 == FFAI_DT_F16, s));
+      kk = base;
+      k_tm = false;
+      kcap = Nk;
+      base += kv_elems;
+    }
+    if (stage_v) {
+      FFAI_CUDA(ctx, launch_to_16bit_heads_split(v, d->kv_dtype, strides_of(d->v_layout, H, cap), B,
+                                                 H, Nk, base, dt16 == FFAI_DT_F16, s));
+      vv = base;
+      v_tm = false;
+      vcap = Nk;
+    }
+  }
+  const int ab_f16 = dt16 == FFAI_DT_F16;
+
+  std::vector<int> qs(B), ql(B, Nq), ks(B), kl(B, Nk);
+  for (int b = 0; b < B; ++b) {
+    qs[b] = b * Nq;
+    ks[b] = b * cap;  // token-major K/V are never staged, so they keep `cap`
+  }
+  int st = prepare_work(ctx, qs, ql, ks, kl, H, s);
+  if (st) return st;
+  const long long BH = static_cast<long long>(B) * H;
+  Operand oq{qq, q_tm, q_tm ? static_cast<long long>(B) * Nq : Nq, BH};
+  Operand ok{kk, k_tm, k_tm ? static_cast<long long>(B) * kcap : kcap, BH};
+  Operand ov{vv, v_tm, v_tm ? static_cast<long long>(B) * vcap : vcap, BH};
+  return run_tc(ctx, oq, ok, ov, H, ab_f16, o, d->out_dtype == FFAI_DT_BF16,
+                d->out_layout == FFAI_LAYOUT_TOKEN_MAJOR, Nq, lse, static_cast<long long>(B) * Nq,
+                d->scale, s);
+}
+
+int decode_impl(ffai_attn_ctx* ctx, const ffai_attn_desc* d, const void* q, const void* k,
+                const void* v, void* o, float* lse, int num_splits, cudaStream_t s) {
+  const int rows = d->batch * d->heads;
+  const int cap = d->kv_capacity > 0 ? d->kv_capacity : d->kv_len;
+  int kv = d->kv_len;
+  if (d->causal) kv = std::min(kv, d->q_offset + 1);
+  if (kv <= 0) return set_error(ctx, FFAI_ATTN_ERR_INVALID, "no visible keys");
+  for (const void* ptr : {q, k, v, static_cast<const void*>(o)})
+    if (reinterpret_cast<uintptr_t>(ptr) % 16 != 0)
+      return set_error(ctx, FFAI_ATTN_ERR_INVALID, "decode operands must be 16-byte aligned");
+  int chunk;
+  if (num_splits > 0) {
+    chunk = (kv + num_splits - 1) / num_splits;
+    chunk = std::min(std::max(chunk, 1), 128);
+  } else {
+    chunk = d->kv_dtype == FFAI_DT_F32 ? 64 : 128;
+    const int splits128 = (kv + chunk - 1) / chunk;
+    if (chunk == 128 && static_cast<long long>(rows) * splits128 < 2LL * ctx->num_sms && kv > 64)
+      chunk = 64;
+  }
+  const int splits = (kv + chunk - 1) / chunk;
+  DecodeParams p{};
+  p.q = q;
+  p.k = k;
+  p.v = v;
+  p.out = o;
+  p.lse = lse;
+  p.rows = rows;
+  p.kv_len = kv;
+  p.cap = cap;
+  p.chunk = chunk;
+  p.splits = splits;
+  p.q_dtype = d->q_dtype;
+  p.kv_dtype = d->kv_dtype;
+  p.out_dtype = d->out_dtype;
+  p.k_kt = d->k_layout == FFAI_LAYOUT_KT;
+  p.scale_log2 = d->scale * 1.4426950408889634f;
+  if (splits > 1) {
+    int st = ensure(ctx, &ctx->d_part, &ctx->part_cap,
+                    static_cast<size_t>(rows) * splits * kPartStride);
+    if (st) return st;
+    st = ensure(ctx, &ctx->d_counters, &ctx->counters_cap, static_cast<size_t>(rows), true);
+    if (st) return st;
+    p.part = ctx->d_part;
+    p.counters = ctx->d_counters;
+  }
+  FFAI_CUDA(ctx, launch_decode(p, s));
+  return FFAI_ATTN_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+const char* ffai_attn_version(void) { return "ffai-attn-b200 1 sm_100a"; }
+
+void ffai_attn_desc_init(ffai_attn_desc* d) {
+  if (!d) return;
+  std::memset(d, 0, sizeof *d);
+  d->batch = 1;
+  d->heads = 1;
+  d->q_len = 1;
+  d->kv_len = 1;
+  d->head_dim = kHD;
+  d->q_dtype = d->kv_dtype = d->out_dtype = FFAI_DT_F32;
+  d->q_layout = d->k_layout = d->v_layout = d->out_layout = FFAI_LAYOUT_HEADS_SPLIT;
+  d->scale = 1.0f;
+}
+
+int ffai_attn_check(const ffai_attn_desc* d, int op) {
+  if (op < FFAI_OP_PREFILL || op > FFAI_OP_VARLEN)
+    return set_error(nullptr, FFAI_ATTN_ERR_INVALID, "unknown op %d", op);
+  return check_desc(nullptr, d, op);
+}
+
+ffai_attn_ctx* ffai_attn_create(int device, int* status) {
+  auto fail = [&](int st) -> ffai_attn_ctx* {
+    if (status) *status = st;
+    return nullptr;
+  };
+  int n = 0;
+  if (cudaGetDeviceCount(&n) != cudaSuccess || n <= 0) {
+    cudaGetLastError();
+    set_error(nullptr, FFAI_ATTN_ERR_NO_DEVICE, "no CUDA device");
+    return fail(FFAI_ATTN_ERR_NO_DEVICE);
+  }
+  if (device < 0 || device >= n) {
+    set_error(nullptr, FFAI_ATTN_ERR_INVALID, "device %d out of range [0,%d)", device, n);
+    return fail(FFAI_ATTN_ERR_INVALID);
+  }
+  DeviceGuard g(device);
+  if (!g.ok) {
+    set_error(nullptr, FFAI_ATTN_ERR_CUDA, "cudaSetDevice(%d) failed", device);
+    return fail(FFAI_ATTN_ERR_CUDA);
+  }
+  cudaDeviceProp prop{};
+  if (cudaGetDeviceProperties(&prop, device) != cudaSuccess || prop.major != 10) {
+    set_error(nullptr, FFAI_ATTN_ERR_NO_DEVICE, "device %d is sm_%d%d; this library is sm_100a",
+              device, prop.major, prop.minor);
+    return fail(FFAI_ATTN_ERR_NO_DEVICE);
+  }
+  std::call_once(g_encode_once, init_encoder);
+  auto* ctx = new ffai_attn_ctx();
+  ctx->device = device;
+  ctx->num_sms = prop.multiProcessorCount;
+  if (cudaMalloc(&ctx->d_err, sizeof(unsigned)) != cudaSuccess ||
+      cudaMemset(ctx->d_err, 0, sizeof(unsigned)) != cudaSuccess) {
+    delete ctx;
+    set_error(nullptr, FFAI_ATTN_ERR_NOMEM, "error word allocation failed");
+    return fail(FFAI_ATTN_ERR_NOMEM);
+  }
+  if (status) *status = FFAI_ATTN_OK;
+  return ctx;
+}
+
+void ffai_attn_destroy(ffai_attn_ctx* ctx) {
+  if (!ctx) return;
+  DeviceGuard g(ctx->device);
+  cudaDeviceSynchronize();
+  if (ctx->pipe_ctx) ffai_attn_destroy(ctx->pipe_ctx);
+  cudaFree(ctx->d_err);
+  cudaFree(ctx->d_part);
+  cudaFree(ctx->d_counters);
+  cudaFree(ctx->d_units);
+  cudaFree(ctx->d_seq);
+  cudaFree(ctx->d_stage);
+  cudaFree(ctx->d_pipe);
+  for (int i = 0; i < 2; ++i) {
+    if (ctx->ev_h2d[i]) cudaEventDestroy(ctx->ev_h2d[i]);
+    if (ctx->ev_comp[i]) cudaEventDestroy(ctx->ev_comp[i]);
+    if (ctx->ev_d2h[i]) cudaEventDestroy(ctx->ev_d2h[i]);
+  }
+  if (ctx->s_h2d) cudaStreamDestroy(ctx->s_h2d);
+  if (ctx->s_comp) cudaStreamDestroy(ctx->s_comp);
+  if (ctx->s_d2h) cudaStreamDestroy(ctx->s_d2h);
+  delete ctx;
+}
+
+int ffai_attn_prefill(ffai_attn_ctx* ctx, const ffai_attn_desc* d, const void* q, const void* k,
+                      const void* v, void* o, float* lse, void* stream) {
+  if (!ctx) return set_error(nullptr, FFAI_ATTN_ERR_INVALID, "null context");
+  const int st = check_desc(ctx, d, FFAI_OP_PREFILL);
+  if (st) return st;
+  if (!q || !k || !v || !o) return set_error(ctx, FFAI_ATTN_ERR_INVALID, "null operand");
+  DeviceGuard g(ctx->device);
+  return prefill_impl(ctx, d, q, k, v, o, lse, static_cast<cudaStream_t>(stream));
+}
+
+int ffai_attn_decode(ffai_attn_ctx* ctx, const ffai_attn_desc* d, const void* q, const void* k,
+                     const void* v, void* o, float* lse, int32_t num_splits, void* stream) {
+  if (!ctx) return set_error(nullptr, FFAI_ATTN_ERR_INVALID, "null context");
+  const int st = check_desc(ctx, d, FFAI_OP_DECODE);
+  if (st) return st;
+  if (!q || !k || !v || !o) return set_error(ctx, FFAI_ATTN_ERR_INVALID, "null operand");
+  DeviceGuard g(ctx->device);
+  return decode_impl(ctx, d, q, k, v, o, lse, num_splits, static_cast<cudaStream_t>(stream));
+}
+
+int ffai_attn_varlen(ffai_attn_ctx* ctx, const ffai_attn_desc* d, const int32_t* cu_q,
+                     const int32_t* cu_k, int32_t n_seg, const void* q, const void* k,
+                     const void* v, void* o, float* lse, void* stream) {
+  if (!ctx) return set_error(nullptr, FFAI_ATTN_ERR_INVALID, "null context");
+  int st = check_desc(ctx, d, FFAI_OP_VARLEN);
+  if (st) return st;
+  if (!cu_q || !cu_k || n_seg <= 0 || !q || !k || !v || !o)
+    return set_error(ctx, FFAI_ATTN_ERR_INVALID, "varlen: null argument or n_seg <= 0");
+  std::vector<int> qs(n_seg), ql(n_seg), ks(n_seg), kl(n_seg);
+  for (int i = 0; i < n_seg; ++i) {
+    qs[i] = cu_q[i];
+    ql[i] = cu_q[i + 1] - cu_q[i];
+    ks[i] = cu_k[i];
+    kl[i] = cu_k[i + 1] - cu_k[i];
+    if (ql[i] < 0 || kl[i] < 0 || cu_q[i] < 0 || cu_k[i] < 0)
+      return set_error(ctx, FFAI_ATTN_ERR_INVALID, "varlen: cu_seqlens must be non-decreasing");
+    if (ql[i] > 0 && kl[i] == 0)
+      return set_error(ctx, FFAI_ATTN_ERR_INVALID, "varlen: segment %d has queries but no keys", i);
+  }
+  const long long Tq = cu_q[n_seg], Tk = cu_k[n_seg];
+  DeviceGuard g(ctx->device);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  st = prepare_work(ctx, qs, ql, ks, kl, d->heads, s);
+  if (st) return st;
+  if (Tq == 0) return FFAI_ATTN_OK;
+  const Operand oq{q, true, Tq, 1}, ok{k, true, Tk, 1}, ov{v, true, Tk, 1};
+  return run_tc(ctx, oq, ok, ov, d->heads, d->q_dtype == FFAI_DT_F16, o,
+                d->out_dtype == FFAI_DT_BF16, true, 0, lse, Tq, d->scale, s);
+}
+
+int ffai_attn_prefill_host(ffai_attn_ctx* ctx, const ffai_attn_desc* d, const void* q,
+                           const void* k, const void* v, void* o, float* lse) {
+  if (!ctx) return set_error(nullptr, FFAI_ATTN_ERR_INVALID, "null context");
+  int st = check_desc(ctx, d, FFAI_OP_PREFILL);
+  if (st) return st;
+  if (!q || !k || !v || !o) return set_error(ctx, FFAI_ATTN_ERR_INVALID, "null operand");
+  DeviceGuard g(ctx->device);
+  if (!ctx->s_h2d) {
+    FFAI_CUDA(ctx, cudaStreamCreateWithFlags(&ctx->s_h2d, cudaStreamNonBlocking));
+    FFAI_CUDA(ctx, cudaStreamCreateWithFlags(&ctx->s_comp, cudaStreamNonBlocking));
+    FFAI_CUDA(ctx, cudaStreamCreateWithFlags(&ctx->s_d2h, cudaStreamNonBlocking));
+    for (int i = 0; i < 2; ++i) {
+      FFAI_CUDA(ctx, cudaEventCreateWithFlags(&ctx->ev_h2d[i], cudaEventDisableTiming));
+      FFAI_CUDA(ctx, cudaEventCreateWithFlags(&ctx->ev_comp[i], cudaEventDisableTiming));
+      FFAI_CUDA(ctx, cudaEventCreateWithFlags(&ctx->ev_d2h[i], cudaEventDisableTiming));
+    }
+  }
+  if (!ctx->pipe_ctx) {
+    int cst = 0;
+    ctx->pipe_ctx = ffai_attn_create(ctx->device, &cst);
+    if (!ctx->pipe_ctx) return set_error(ctx, cst, "pipeline context: %s", g_tls_error.c_str());
+  }
+  const int B = d->batch, H = d->heads, Nq = d->q_len;
+  const int cap = d->kv_capacity > 0 ? d->kv_capacity : d->kv_len;
+  // Per-sequence byte sizes: every layout keeps one sequence contiguous.
+  const size_t qb = static_cast<size_t>(H) * Nq * kHD * dtype_size(d->q_dtype);
+  const size_t kb = static_cast<size_t>(H) * cap * kHD * dtype_size(d->kv_dtype);
+  const size_t ob = static_cast<size_t>(H) * Nq * kHD * dtype_size(d->out_dtype);
+  const size_t lb = lse ? static_cast<size_t>(H) * Nq * sizeof(float) : 0;
+  if (lse && d->out_layout == FFAI_LAYOUT_TOKEN_MAJOR)
+    return set_error(ctx, FFAI_ATTN_DECLINED, "host prefill: lse needs heads-split output");
+  // Chunks of sequences, two slots in flight.
+  const int chunk = std::max(1, std::min(B, (B + 3) / 4));
+  const size_t slot = chunk * (qb + 2 * kb + ob + lb);
+  const size_t slot_al = (slot + 255) / 256 * 256;
+  st = ensure(ctx, reinterpret_cast<uint8_t**>(&ctx->d_pipe), &ctx->pipe_cap, 2 * slot_al);
+  if (st) return st;
+  uint8_t* dev = static_cast<uint8_t*>(ctx->d_pipe);
+  const uint8_t* hq = static_cast<const uint8_t*>(q);
+  const uint8_t* hk = static_cast<const uint8_t*>(k);
+  const uint8_t* hv = static_cast<const uint8_t*>(v);
+  uint8_t* ho = static_cast<uint8_t*>(o);
+  uint8_t* hl = reinterpret_cast<uint8_t*>(lse);
+  const int nchunks = (B + chunk - 1) / chunk;
+  // Fresh state for every call: the previous call's last D2H completed before it returned.
+  for (int c = 0; c < nchunks; ++c) {
+    const int b0 = c * chunk;
+    const int nb = std::min(chunk, B - b0);
+    const int sl = c % 2;
+    uint8_t* base = dev + sl * slot_al;
+    uint8_t* dq = base;
+    uint8_t* dk = dq + chunk * qb;
+    uint8_t* dv = dk + chunk * kb;
+    uint8_t* do_ = dv + chunk * kb;
+    uint8_t* dl = do_ + chunk * ob;
+    if (c >= 2) FFAI_CUDA(ctx, cudaStreamWaitEvent(ctx->s_h2d, ctx->ev_d2h[sl], 0));
+    FFAI_CUDA(ctx, cudaMemcpyAsync(dq, hq + b0 * qb, nb * qb, cudaMemcpyHostToDevice, ctx->s_h2d));
+    FFAI_CUDA(ctx, cudaMemcpyAsync(dk, hk + b0 * kb, nb * kb, cudaMemcpyHostToDevice, ctx->s_h2d));
+    FFAI_CUDA(ctx, cudaMemcpyAsync(dv, hv + b0 * kb, nb * kb, cudaMemcpyHostToDevice, ctx->s_h2d));
+    FFAI_CUDA(ctx, cudaEventRecord(ctx->ev_h2d[sl], ctx->s_h2d));
+    FFAI_CUDA(ctx, cudaStreamWaitEvent(ctx->s_comp, ctx->ev_h2d[sl], 0));
+    ffai_attn_desc dc = *d;
+    dc.batch = nb;
+    st = prefill_impl(ctx->pipe_ctx, &dc, dq, dk, dv, do_, lse ? reinterpret_cast<float*>(dl) : nullptr,
+                      ctx->s_comp);
+    if (st) return set_error(ctx, st, "%s", ctx->pipe_ctx->last_error.c_str());
+    FFAI_CUDA(ctx, cudaEventRecord(ctx->ev_comp[sl], ctx->s_comp));
+    FFAI_CUDA(ctx, cudaStreamWaitEvent(ctx->s_d2h, ctx->ev_comp[sl], 0));
+    FFAI_CUDA(ctx, cudaMemcpyAsync(ho + b0 * ob, do_, nb * ob, cudaMemcpyDeviceToHost, ctx->s_d2h));
+    if (lse)
+      FFAI_CUDA(ctx, cudaMemcpyAsync(hl + b0 * lb, dl, nb * lb, cudaMemcpyDeviceToHost, ctx->s_d2h));
+    FFAI_CUDA(ctx, cudaEventRecord(ctx->ev_d2h[sl], ctx->s_d2h));
+  }
+  FFAI_CUDA(ctx, cudaStreamSynchronize(ctx->s_d2h));
+  unsigned err = 0;
+  FFAI_CUDA(ctx, cudaMemcpy(&err, ctx->pipe_ctx->d_err, sizeof err, cudaMemcpyDeviceToHost));
+  if (err) {
+    cudaMemset(ctx->pipe_ctx->d_err, 0, sizeof(unsigned));
+    return set_error(ctx, FFAI_ATTN_ERR_TIMEOUT, "in-kernel wait timed out (error bits 0x%x)", err);
+  }
+  return FFAI_ATTN_OK;
+}
+
+int ffai_attn_sync(ffai_attn_ctx* ctx, void* stream) {
+  if (!ctx) return set_error(nullptr, FFAI_ATTN_ERR_INVALID, "null context");
+  DeviceGuard g(ctx->device);
+  FFAI_CUDA(ctx, cudaStreamSynchronize(static_cast<cudaStream_t>(stream)));
+  unsigned err = 0;
+  FFAI_CUDA(ctx, cudaMemcpy(&err, ctx->d_err, sizeof err, cudaMemcpyDeviceToHost));
+  if (err) {
+    FFAI_CUDA(ctx, cudaMemset(ctx->d_err, 0, sizeof(unsigned)));
+    return set_error(ctx, FFAI_ATTN_ERR_TIMEOUT, "in-kernel wait timed out (error bits 0x%x)", err);
+  }
+  return FFAI_ATTN_OK;
+}
+
+int ffai_attn_last_error(const ffai_attn_ctx* ctx, char* buf, size_t n) {
+  const std::string& msg = ctx ? ctx->last_error : g_tls_error;
+  const int st = ctx ? ctx->last_status : g_tls_status;
+  if (buf && n) {
+    std::strncpy(buf, msg.c_str(), n - 1);
+    buf[n - 1] = 0;
+  }
+  return st;
+}
+
+// ---------------------------------------------------------------------------
+// The reference's custom-op surface (flash_attn.rs:104-264), mirrored.
+// ---------------------------------------------------------------------------
+
+int ffai_flash_serves(const ffai_tensor4* kt, const ffai_tensor4* v) {
+  if (!kt || !v || kt->device < 0 || v->device < 0) return 0;
+  // (1, h1, 64, keys) and (1, h2, keys, 64), same heads and keys, and keys at
+  // or above the floor the consumer applies (flash_attn.rs:112-128).
+  if (kt->dims[0] != 1 || kt->dims[2] != kHD || v->dims[0] != 1 || v->dims[3] != kHD) return 0;
+  const int64_t keys = kt->dims[3];
+  return (kt->dims[1] == v->dims[1] && keys == v->dims[2] &&
+          keys >= std::max(kMinSeq, min_decode_keys()))
+             ? 1
+             : 0;
+}
+
+namespace {
+
+int attend_common(ffai_attn_ctx* ctx, const ffai_tensor4* q, const ffai_tensor4* kt,
+                  const ffai_tensor4* v, int masked, ffai_tensor4* out, bool merged, void* stream) {
+  if (!ctx) return set_error(nullptr, FFAI_ATTN_ERR_INVALID, "null context");
+  if (!q || !kt || !v || !out) return set_error(ctx, FFAI_ATTN_ERR_INVALID, "null tensor");
+  if (masked) return set_error(ctx, FFAI_ATTN_DECLINED, "masked attention is not served");
+  if (q->device != ctx->device || kt->device != ctx->device || v->device != ctx->device ||
+      out->device != ctx->device)
+    return set_error(ctx, FFAI_ATTN_DECLINED, "operands are not on this context's CUDA device");
+  if (q->dtype != FFAI_DT_F32) return set_error(ctx, FFAI_ATTN_DECLINED, "q must be f32");
+  const int64_t b = q->dims[0], heads = q->dims[1], qlen = q->dims[2], hd = q->dims[3];
+  if (b != 1 || hd != kHD) return set_error(ctx, FFAI_ATTN_DECLINED, "batch 1, head_dim 64 only");
+  if (kt->dims[0] != 1 || kt->dims[1] != heads || kt->dims[2] != kHD)
+    return set_error(ctx, FFAI_ATTN_DECLINED, "kt must be (1,H,64,keys)");
+  const int64_t keys = kt->dims[3];
+  if (v->dims[0] != 1 || v->dims[1] != heads || v->dims[2] != keys || v->dims[3] != kHD)
+    return set_error(ctx, FFAI_ATTN_DECLINED, "v must be (1,H,keys,64)");
+  if (kt->dtype != v->dtype) return set_error(ctx, FFAI_ATTN_DECLINED, "k/v dtypes differ");
+  const bool half_kv = kt->dtype != FFAI_DT_F32;
+  if (half_kv && (qlen != 1 || merged))
+    return set_error(ctx, FFAI_ATTN_DECLINED, "f16/bf16 K/V is served at the decode shape only");
+  const int64_t floor = qlen == 1 && !merged ? min_decode_keys() : kMinSeq;
+  if (keys < floor)
+    return set_error(ctx, FFAI_ATTN_DECLINED, "%lld keys below the floor %lld",
+                     static_cast<long long>(keys), static_cast<long long>(floor));
+  if (merged ? qlen != keys : (qlen != 1 && qlen != keys))
+    return set_error(ctx, FFAI_ATTN_DECLINED, "q_len %lld not served against %lld keys",
+                     static_cast<long long>(qlen), static_cast<long long>(keys));
+  if (out->dtype != FFAI_DT_F32) return set_error(ctx, FFAI_ATTN_ERR_INVALID, "out must be f32");
+
+  ffai_attn_desc d;
+  ffai_attn_desc_init(&d);
+  d.heads = static_cast<int32_t>(heads);
+  d.q_len = static_cast<int32_t>(qlen);
+  d.kv_len = static_cast<int32_t>(keys);
+  d.q_dtype = FFAI_DT_F32;
+  d.kv_dtype = kt->dtype;
+  d.k_layout = FFAI_LAYOUT_KT;
+  d.out_layout = merged ? FFAI_LAYOUT_TOKEN_MAJOR : FFAI_LAYOUT_HEADS_SPLIT;
+  d.scale = 1.0f;  // q arrives pre-scaled (flash_attn.rs:214-217)
+  if (env_on("FFAI_ATTN_CHECKED_F32")) d.flags |= FFAI_ATTN_FLAG_CHECKED_F32;
+  if (qlen == 1 && !merged)
+    return ffai_attn_decode(ctx, &d, q->data, kt->data, v->data, out->data, nullptr, 0, stream);
+  return ffai_attn_prefill(ctx, &d, q->data, kt->data, v->data, out->data, nullptr, stream);
+}
+
+}  // namespace
+
+int ffai_flash_attend(ffai_attn_ctx* ctx, const ffai_tensor4* q, const ffai_tensor4* kt,
+                      const ffai_tensor4* v, int32_t masked, ffai_tensor4* out, void* stream) {
+  return attend_common(ctx, q, kt, v, masked, out, false, stream);
+}
+
+int ffai_flash_attend_merged(ffai_attn_ctx* ctx, const ffai_tensor4* q, const ffai_tensor4* kt,
+                             const ffai_tensor4* v, ffai_tensor4* out, void* stream) {
+  return attend_common(ctx, q, kt, v, 0, out, true, stream);
+}
+
+}  // extern "C"

@@ -1,0 +1,106 @@
+// Internal interface between the C ABI (api.cu) and the kernels.  Plain
+// structs of device pointers and sizes; no torch or candle types.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace ffai {
+
+// ---- decode (decode.cu) ----------------------------------------------------
+
+constexpr int kPartStride = 66;  // per (row, split): m, l, o[64]
+
+struct DecodeParams {
+  const void* q;  // (rows, 64) of q_dtype
+  const void* k;  // rows x cap x 64 (row-major) or rows x 64 x cap (KT)
+  const void* v;  // rows x cap x 64
+  void* out;      // (rows, 64) f32 or bf16
+  float* lse;     // (rows) or null
+  float* part;    // rows x splits x kPartStride   (splits > 1)
+  unsigned* counters;  // rows tickets, zero between launches (splits > 1)
+  int rows;
+  int kv_len;
+  int cap;
+  int chunk;   // keys per CTA, <= 128
+  int splits;  // ceil(kv_len / chunk)
+  int q_dtype, kv_dtype, out_dtype;
+  int k_kt;
+  float scale_log2;
+};
+
+cudaError_t launch_decode(const DecodeParams& p, cudaStream_t s);
+
+// ---- checked f32 prefill (prefill_simt.cu) ---------------------------------
+
+// Element offset of (b, h, row, d) is b*sb + h*sh + row*sr + d*sd.
+struct Strides {
+  long long sb, sh, sr, sd;
+};
+
+struct SimtParams {
+  const float* q;
+  const float* k;
+  const float* v;
+  void* out;
+  float* lse;  // indexed by b*lse_sb + h*lse_sh + row, or null
+  Strides qs, ks, vs, os;
+  long long lse_sb, lse_sh;
+  int B, H, Nq, Nk;
+  int out_dtype;
+  int causal, q_offset;
+  float scale;
+};
+
+cudaError_t launch_prefill_simt(const SimtParams& p, cudaStream_t s);
+
+// ---- tensor-core prefill (prefill_tc.cu) -----------------------------------
+
+constexpr int kTcRows = 128;    // query rows per tile (MMA M)
+constexpr int kTcKeys = 128;    // keys per block (MMA N of Q.K^T)
+constexpr int kTcStages = 3;    // K/V ring depth
+constexpr int kTcThreads = 320; // 2 softmax warpgroups + TMA warp + MMA warp
+
+// One work unit: query rows [row0, row0 + 128*ntiles) of (seq, head).
+struct TcUnit {
+  int seq, head, row0, ntiles;
+};
+
+struct TcParams {
+  const int4* units;  // TcUnit as int4
+  int num_units;
+  const int* q_start;  // per sequence: first packed token (token-major) or 0
+  const int* q_len;
+  const int* k_start;
+  const int* k_len;
+  int heads;
+  int q_token_major;   // 0: map coords {0,row,seq*H+head}; 1: {0,head,q_start+row}
+  int k_token_major;
+  int v_token_major;
+  void* out;
+  int out_bf16;
+  int out_token_major;
+  long long out_rows;  // heads-split output: rows per (seq, head)
+  float* lse;
+  long long lse_tokens;  // token-major lse is (H, lse_tokens)
+  float scale_log2;
+  unsigned* err;
+};
+
+// tm*: 3-d tensor maps built by the host for 128-row x 64-col boxes with
+// 128-byte swizzle.  ab_f16: 1 for f16 operands, 0 for bf16.
+cudaError_t launch_prefill_tc(const CUtensorMap& tmQ, const CUtensorMap& tmK,
+                              const CUtensorMap& tmV, const TcParams& p, int grid, int ab_f16,
+                              cudaStream_t s);
+size_t prefill_tc_smem_bytes();
+
+// ---- conversions (convert.cu) -----------------------------------------------
+
+// dst (B,H,N,64) heads-split contiguous 16-bit (bf16, or f16 when dst_f16)
+// <- src element (b,h,row,d) at b*sb + h*sh + row*sr + d*sd of f32 / bf16 /
+// f16 (src_dtype 0/1/2).
+cudaError_t launch_to_16bit_heads_split(const void* src, int src_dtype, Strides st, int B, int H,
+                                        int N, void* dst, int dst_f16, cudaStream_t s);
+
+}  // namespace ffai

@@ -1,0 +1,199 @@
+/*
+ * ffai_attn.h -- C ABI of the B200 Whisper attention library (libffai_attn.so).
+ *
+ * This library replaces the fused CPU attention of the reference,
+ * crates/ffai-mercury/src/asr/flash_attn.rs (Remade-With-Rust/FFAI 0.6.2):
+ * encoder self-attention, decoder self-attention over the KV cache, and
+ * decoder cross-attention.  A Rust crate binds these functions with
+ * `extern "C"` declarations; nothing here names a Rust, candle or torch type.
+ *
+ * Conventions shared by every entry point:
+ *   - Status: FFAI_ATTN_OK (0) served; FFAI_ATTN_DECLINED (1) the shape is not
+ *     one this library serves and the caller should take its fallback path
+ *     (the reference's `Ok(None)`, flash_attn.rs:135-158, :218-264); negative
+ *     values are errors (the reference's `Err`, e.g. the `bail!`s at
+ *     flash_attn.rs:181-185, :359-363).  ffai_attn_last_error() describes the
+ *     last error or decline of a context.
+ *   - Buffers are caller-owned device pointers unless a function says host.
+ *   - `stream` is a cudaStream_t passed as void* (NULL = legacy default stream).
+ *   - One context per device.  Calls on one context must not overlap on the
+ *     GPU (the context owns one workspace): serialise them, as the reference's
+ *     engine does behind its Mutex (whisper_candle.rs:50-51, :222).
+ *   - head_dim is 64 (every Whisper size; flash_attn.rs:50).
+ */
+#ifndef FFAI_ATTN_H
+#define FFAI_ATTN_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define FFAI_ATTN_ABI_VERSION 1
+
+/* ---- status codes ---- */
+#define FFAI_ATTN_OK 0
+#define FFAI_ATTN_DECLINED 1
+#define FFAI_ATTN_ERR_INVALID (-1)  /* malformed descriptor or pointer */
+#define FFAI_ATTN_ERR_CUDA (-2)     /* a CUDA runtime/driver call failed */
+#define FFAI_ATTN_ERR_TIMEOUT (-3)  /* a bounded in-kernel wait gave up */
+#define FFAI_ATTN_ERR_NOMEM (-4)    /* workspace allocation failed */
+#define FFAI_ATTN_ERR_NO_DEVICE (-5)
+
+/* ---- element types ---- */
+#define FFAI_DT_F32 0
+#define FFAI_DT_BF16 1
+#define FFAI_DT_F16 2
+
+/* ---- layouts (B = batch of independent sequences, H = heads, N = rows) ----
+ * HEADS_SPLIT  (B, H, N, 64): the reference's q and v layout (flash_attn.rs:212-217).
+ * TOKEN_MAJOR  (B, N, H, 64), i.e. the merged (B, N, H*64) layout that
+ *              attend_merged returns (flash_attn.rs:131-134); also the packed
+ *              layout of the variable-length entry point, (T, H, 64).
+ * KT           (B, H, 64, N): K transposed, head-dim major, as the reference's
+ *              callers hand it over (text_decoder.rs:1107-1114).  K only.     */
+#define FFAI_LAYOUT_HEADS_SPLIT 0
+#define FFAI_LAYOUT_TOKEN_MAJOR 1
+#define FFAI_LAYOUT_KT 2
+
+/* ---- flags ---- */
+/* Run the f32 SIMT kernel (f32 operands only) instead of the bf16 tensor-core
+ * kernel: max relative error 1e-5 instead of the bf16 path's 1e-2 abs. */
+#define FFAI_ATTN_FLAG_CHECKED_F32 0x1u
+
+/* ---- operations, for ffai_attn_check ---- */
+#define FFAI_OP_PREFILL 0
+#define FFAI_OP_DECODE 1
+#define FFAI_OP_VARLEN 2
+
+typedef struct ffai_attn_desc {
+  int32_t batch;       /* independent sequences: segments or beams          */
+  int32_t heads;       /* heads per sequence                                */
+  int32_t q_len;       /* query rows per (sequence, head)                   */
+  int32_t kv_len;      /* keys per (sequence, head) that are attended       */
+  int32_t head_dim;    /* must be 64                                        */
+  int32_t kv_capacity; /* allocated keys per (sequence, head) in k and v;
+                          0 means kv_len.  A KV cache of capacity 448 can be
+                          attended at its current length kv_len <= 448.     */
+  int32_t q_dtype;     /* FFAI_DT_*                                         */
+  int32_t kv_dtype;    /* FFAI_DT_*                                         */
+  int32_t out_dtype;   /* FFAI_DT_F32 or FFAI_DT_BF16                       */
+  int32_t q_layout;    /* FFAI_LAYOUT_*                                     */
+  int32_t k_layout;
+  int32_t v_layout;
+  int32_t out_layout;  /* HEADS_SPLIT or TOKEN_MAJOR                        */
+  int32_t causal;      /* 1: key j visible to row i iff j <= q_offset + i   */
+  int32_t q_offset;
+  float scale;         /* logits = scale * q.k; the reference folds it into
+                          q before the kernel, so its callers pass 1.0      */
+  uint32_t flags;      /* FFAI_ATTN_FLAG_*                                  */
+} ffai_attn_desc;
+
+typedef struct ffai_attn_ctx ffai_attn_ctx;
+
+/* Library version string, e.g. "ffai-attn-b200 1 sm_100a". */
+const char* ffai_attn_version(void);
+
+/* Fill `d` with defaults: batch 1, head_dim 64, f32 everywhere, heads-split
+ * layouts, scale 1.0, no flags. */
+void ffai_attn_desc_init(ffai_attn_desc* d);
+
+/* Host-only shape/dtype gate: FFAI_ATTN_OK if `op` serves `d`, else
+ * FFAI_ATTN_DECLINED or FFAI_ATTN_ERR_INVALID.  Needs no GPU. */
+int ffai_attn_check(const ffai_attn_desc* d, int op);
+
+/* Create a context on CUDA device `device` (workspace, device error word,
+ * TMA descriptor encoder).  Replaces the reference's lazy CPU feature
+ * detection (flash_attn.rs:75-97).  Returns NULL and sets *status on error. */
+ffai_attn_ctx* ffai_attn_create(int device, int* status);
+void ffai_attn_destroy(ffai_attn_ctx* ctx);
+
+/* Encoder/prefill attention over `batch` equal-length sequences:
+ *   o = softmax(scale * q k^T) v per (sequence, head).
+ * Replaces MergedAttnOp::cpu_fwd / FlashAttnOp::cpu_fwd's encoder branch
+ * (flash_attn.rs:170-209, :400-405) and flash_head_strided (:429-487).
+ * bf16/f16 operands run the tcgen05 tensor-core kernel; f32 operands are
+ * converted to bf16 on the device first, unless FFAI_ATTN_FLAG_CHECKED_F32
+ * selects the f32 SIMT kernel.  `lse` (optional, f32) receives the natural
+ * log-sum-exp of each row's scaled logits: (B,H,N) for heads-split output,
+ * (H, B*N) for token-major output. */
+int ffai_attn_prefill(ffai_attn_ctx* ctx, const ffai_attn_desc* d, const void* q, const void* k,
+                      const void* v, void* o, float* lse, void* stream);
+
+/* Decode attention, q_len = 1, over batch*heads rows (beams x heads), with
+ * split-KV partial softmax and an in-kernel combine.  Replaces the decode
+ * branch of FlashAttnOp::cpu_fwd (flash_attn.rs:289-399), xattn_head (:602-696)
+ * and xattn_head_f16 (:714-789).  q is f32 or the cache type; the cache (k, v)
+ * is f32, bf16 or f16; k is KT or HEADS_SPLIT (row-major keys); v is
+ * HEADS_SPLIT.  `num_splits` 0 = automatic.  Output (B,H,1,64). */
+int ffai_attn_decode(ffai_attn_ctx* ctx, const ffai_attn_desc* d, const void* q, const void* k,
+                     const void* v, void* o, float* lse, int32_t num_splits, void* stream);
+
+/* Variable-length (ragged) prefill over packed segments, TOKEN_MAJOR
+ * (T, H, 64) operands and output.  Segment s owns query rows
+ * [cu_seqlens_q[s], cu_seqlens_q[s+1]) and keys [cu_seqlens_k[s],
+ * cu_seqlens_k[s+1]); each attends only within itself.  The cu_seqlens arrays
+ * are HOST arrays of n_seg+1 int32 (lengths are known to the host that packed
+ * the buffer); the context schedules the (segment, head, row-tile) work items
+ * longest first.  No reference counterpart: the reference loops windows one
+ * at a time (text_decoder.rs:1069-1076).  d->batch, q_len and kv_len are
+ * ignored; d->heads, dtypes, scale and flags apply.  `lse` is (H, T). */
+int ffai_attn_varlen(ffai_attn_ctx* ctx, const ffai_attn_desc* d, const int32_t* cu_seqlens_q,
+                     const int32_t* cu_seqlens_k, int32_t n_seg, const void* q, const void* k,
+                     const void* v, void* o, float* lse, void* stream);
+
+/* Host-buffer prefill: q, k, v, o (and lse) are HOST pointers (pinned memory
+ * recommended).  The context streams the batch through the device in
+ * sequence chunks, overlapping host-to-device copies, kernels and
+ * device-to-host copies on its own streams, and returns when `o` holds the
+ * result.  This is the end-to-end entry a CPU caller (the reference's
+ * candle CPU tensors) uses.  Same layouts and semantics as
+ * ffai_attn_prefill. */
+int ffai_attn_prefill_host(ffai_attn_ctx* ctx, const ffai_attn_desc* d, const void* q,
+                           const void* k, const void* v, void* o, float* lse);
+
+/* Synchronise `stream` and report the device error word: FFAI_ATTN_OK, or
+ * FFAI_ATTN_ERR_TIMEOUT if an in-kernel bounded wait gave up since the last
+ * call (the word is then cleared), or FFAI_ATTN_ERR_CUDA. */
+int ffai_attn_sync(ffai_attn_ctx* ctx, void* stream);
+
+/* Copy the last error or decline message of `ctx` (or of the calling thread
+ * when ctx is NULL) into buf; returns the status it belongs to. */
+int ffai_attn_last_error(const ffai_attn_ctx* ctx, char* buf, size_t n);
+
+/* ---- the reference's custom-op surface, mirrored ------------------------
+ * A contiguous 4-d tensor as the reference's candle Tensor presents it to
+ * flash_attn.rs.  device = CUDA ordinal, or -1 for host memory. */
+typedef struct ffai_tensor4 {
+  void* data;
+  int64_t dims[4];
+  int32_t dtype;  /* FFAI_DT_* */
+  int32_t device;
+} ffai_tensor4;
+
+/* flash_attn::serves (flash_attn.rs:104-129): 1 if the decode kernel will
+ * serve this K^T (1,H,64,keys) / V (1,H,keys,64) pair, else 0.  Callers use
+ * it to choose the cross-attention cache dtype before building the cache. */
+int ffai_flash_serves(const ffai_tensor4* kt, const ffai_tensor4* v);
+
+/* flash_attn::attend (flash_attn.rs:218-264): q (1,H,qlen,64) pre-scaled f32,
+ * kt (1,H,64,keys), v (1,H,keys,64) f32 (or f16/bf16 at qlen = 1).  Writes
+ * out (1,H,qlen,64) f32.  FFAI_ATTN_DECLINED where the reference returns
+ * Ok(None): masked, head_dim != 64, keys below the floor
+ * (FFAI_DECODE_MIN_KEYS for qlen = 1, 256 otherwise), qlen not in {1, keys},
+ * or host memory. */
+int ffai_flash_attend(ffai_attn_ctx* ctx, const ffai_tensor4* q, const ffai_tensor4* kt,
+                      const ffai_tensor4* v, int32_t masked, ffai_tensor4* out, void* stream);
+
+/* flash_attn::attend_merged (flash_attn.rs:135-158): as attend for the
+ * encoder shape, writing out (1, seq, H*64) f32 directly. */
+int ffai_flash_attend_merged(ffai_attn_ctx* ctx, const ffai_tensor4* q, const ffai_tensor4* kt,
+                             const ffai_tensor4* v, ffai_tensor4* out, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* FFAI_ATTN_H */

@@ -1,0 +1,107 @@
+"""GPU parity of the split-KV decode kernel (q_len = 1) against the oracle's
+restated xattn_head / xattn_head_f16 (flash_attn.rs:602-789), on the decode
+workload's shapes: 5 beams x 12 heads over a KV cache of {1, 32, 128, 448}
+keys (self-attention) and 1500 keys (cross-attention)."""
+
+import numpy as np
+import pytest
+import torch
+
+from ffai_b200 import attention, workloads
+from helpers import (BF16_MAX_ABS, F32_REL, ROWSUM_TOL, assert_bf16_close, assert_f32_close,
+                     f32np, rowsum_error)
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda:0"
+
+
+def _oracle_decode(oracle, q, k, v, scale=1.0):
+    B, H, _, _ = q.shape
+    keys = k.shape[2]
+    qn = f32np(q).reshape(B * H, 64) * np.float32(scale)
+    ktn = np.ascontiguousarray(np.swapaxes(f32np(k).reshape(B * H, keys, 64), 1, 2))
+    vn = f32np(v).reshape(B * H, keys, 64)
+    return oracle.xattn_rows(qn, ktn, vn, threads=8).reshape(B, H, 1, 64)
+
+
+@pytest.mark.parametrize("keys", [1, 7, 8, 32, 128, 448, 1500])
+@pytest.mark.parametrize("k_layout", ["heads", "kt"])
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16, torch.float32])
+def test_decode_parity(oracle, keys, k_layout, dtype):
+    q, k, v = workloads.decode_inputs(keys, seed=1, dtype=dtype)
+    ref = _oracle_decode(oracle, q, k, v)
+    kd = k.transpose(-1, -2).contiguous() if k_layout == "kt" else k
+    out, lse = attention.decode(q.to(DEV), kd.to(DEV), v.to(DEV), k_layout=k_layout, with_lse=True)
+    got = f32np(out)
+    # q stays f32 and products are f32 even over a 16-bit cache, so every
+    # cache dtype meets the checked-f32 bar against the oracle.
+    assert_f32_close(got, ref, f"decode keys={keys} {k_layout} {dtype}")
+    assert_bf16_close(got, ref)
+    B, H = q.shape[:2]
+    err = rowsum_error(f32np(q).reshape(B * H, 1, 64), f32np(k).reshape(B * H, keys, 64), 1.0,
+                       f32np(lse).reshape(B * H, 1))
+    assert err <= ROWSUM_TOL, f"row sums off by {err:.2e}"
+
+
+@pytest.mark.parametrize("splits", [1, 2, 3, 7, 12, 0])
+def test_decode_split_counts(oracle, splits):
+    q, k, v = workloads.decode_inputs(1500, seed=2)
+    ref = _oracle_decode(oracle, q, k, v)
+    out = attention.decode(q.to(DEV), k.to(DEV), v.to(DEV), num_splits=splits)
+    assert_f32_close(f32np(out), ref, f"splits={splits}")
+
+
+def test_decode_cache_prefix(oracle):
+    """A cache of capacity 448 attended at its current length 129."""
+    q, k, v = workloads.decode_inputs(448, seed=3)
+    L = 129
+    ref = _oracle_decode(oracle, q, k[:, :, :L], v[:, :, :L])
+    for layout in ("heads", "kt"):
+        kd = k.transpose(-1, -2).contiguous() if layout == "kt" else k
+        out = attention.decode(q.to(DEV), kd.to(DEV), v.to(DEV), k_layout=layout, kv_len=L)
+        assert_f32_close(f32np(out), ref, f"prefix {layout}")
+    # causal at q_len 1: the query at position q_offset sees keys <= q_offset
+    out = attention.decode(q.to(DEV), k.to(DEV), v.to(DEV), causal=True, q_offset=L - 1)
+    assert_f32_close(f32np(out), ref, "causal prefix")
+
+
+def test_decode_scale_and_bf16_out(oracle):
+    q, k, v = workloads.decode_inputs(448, seed=4)
+    ref = _oracle_decode(oracle, q, k, v, scale=0.125)
+    out = attention.decode(q.to(DEV), k.to(DEV), v.to(DEV), scale=0.125, out_dtype=torch.bfloat16)
+    assert out.dtype == torch.bfloat16
+    assert_bf16_close(f32np(out), ref, "bf16 out")
+
+
+def test_decode_bf16_query(oracle):
+    q, k, v = workloads.decode_inputs(1500, seed=5)
+    qb = q.to(torch.bfloat16)
+    ref = _oracle_decode(oracle, qb, k, v)
+    out = attention.decode(qb.to(DEV), k.to(DEV), v.to(DEV))
+    assert_f32_close(f32np(out), ref, "bf16 q")
+
+
+def test_decode_repeatable_and_ticket_rearmed(oracle):
+    """Back-to-back launches reuse the split tickets; results stay bitwise equal."""
+    q, k, v = workloads.decode_inputs(1500, seed=6)
+    qd, kd, vd = q.to(DEV), k.to(DEV), v.to(DEV)
+    first = attention.decode(qd, kd, vd).clone()
+    for _ in range(5):
+        again = attention.decode(qd, kd, vd)
+        assert torch.equal(first, again)
+    attention.sync(0)
+
+
+def test_decode_beams_independent():
+    """Changing one beam's cache changes only that beam's output."""
+    q, k, v = workloads.decode_inputs(448, seed=7)
+    qd, kd, vd = q.to(DEV), k.to(DEV), v.to(DEV)
+    a = attention.decode(qd, kd, vd).clone()
+    kd2 = kd.clone()
+    kd2[2] = kd2[2].flip(1)
+    vd2 = vd.clone()
+    vd2[2] = torch.roll(vd2[2], 5, 1)
+    b = attention.decode(qd, kd2, vd2)
+    keep = [0, 1, 3, 4]
+    assert torch.equal(a[keep], b[keep])
+    assert not torch.equal(a[2], b[2])
