@@ -339,6 +339,10 @@ def run_ours(args, dist):
     dev = torch.device("cuda", dist.local)
     peaks = load_peaks()
     cfg = workloads.C4
+    if args.segments:
+        # smaller batch of the same shape, for profiler captures (reported in config)
+        cfg = workloads.Encoder(cfg.name + f"-{args.segments}seg", args.segments, cfg.heads,
+                                cfg.seq, cfg.dtype)
     lo, hi = partition.contiguous_ranges(cfg.segments, dist.world)[dist.rank]
     nseg = hi - lo
     seg_bytes = cfg.heads * cfg.seq * 64 * 2
@@ -497,6 +501,8 @@ def main():
     ap.add_argument("--no-decode", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    ap.add_argument("--segments", type=int, default=0,
+                    help="profiling only: run a smaller batch of c4 segments")
     args = ap.parse_args()
     dist = Dist()
     if args.impl == "reference":

@@ -60,7 +60,7 @@ cudaError_t launch_prefill_simt(const SimtParams& p, cudaStream_t s);
 constexpr int kTcRows = 128;    // query rows per tile (MMA M)
 constexpr int kTcKeys = 128;    // keys per block (MMA N of Q.K^T)
 constexpr int kTcStages = 3;    // K/V ring depth
-constexpr int kTcThreads = 320; // 2 softmax warpgroups + TMA warp + MMA warp
+constexpr int kTcThreads = 608; // 4 softmax warpgroups + TMA warp + 2 MMA warps
 
 // One work unit: query rows [row0, row0 + 128*ntiles) of (seq, head).
 struct TcUnit {

@@ -7,7 +7,8 @@
 // <= 1e-5 against the f32 reference) rather than the bf16 tensor-core path.
 //
 // Thread (ty, tx) of the 16x16 CTA owns query rows 4ty..4ty+3 and, for the
-// scores, keys tx+16c (c < 4); for the output, head dims tx+16c.  Shared
+// scores, keys tx+16c (c < 4); for the output, head dims tx+16c.  Each thread
+// also keeps the row sums of its four rows, accumulated in the P.V loop.  Shared
 // tiles are padded to 65 floats per row so every access is bank-conflict free.
 #include "common.cuh"
 #include "kernels.h"
@@ -108,17 +109,10 @@ __global__ void __launch_bounds__(256) prefill_simt_kernel(SimtParams p) {
       const float m_new = fmaxf(m[i], bmax);
       const float corr = (m[i] == -INFINITY) ? 0.f : expf(m[i] - m_new);
       const float m_use = (m_new == -INFINITY) ? 0.f : m_new;
-      float psum = 0.f;
 #pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        const float pv = expf(s[i][c] - m_use);
-        sP[(ty * 4 + i) * kPad + tx + 16 * c] = pv;
-        psum += pv;
-      }
-#pragma unroll
-      for (int off = 8; off > 0; off >>= 1) psum += __shfl_xor_sync(0xffffffffu, psum, off);
-      l[i] = l[i] * corr + psum;
+      for (int c = 0; c < 4; ++c) sP[(ty * 4 + i) * kPad + tx + 16 * c] = expf(s[i][c] - m_use);
       m[i] = m_new;
+      l[i] *= corr;
 #pragma unroll
       for (int c = 0; c < 4; ++c) o[i][c] *= corr;
     }
@@ -132,9 +126,14 @@ __global__ void __launch_bounds__(256) prefill_simt_kernel(SimtParams p) {
 #pragma unroll
       for (int c = 0; c < 4; ++c) vv[c] = sV[j * kPad + tx + 16 * c];
 #pragma unroll
-      for (int i = 0; i < 4; ++i)
+      for (int i = 0; i < 4; ++i) {
 #pragma unroll
         for (int c = 0; c < 4; ++c) o[i][c] = fmaf(pv[i], vv[c], o[i][c]);
+        // The normaliser accumulates the same products in the same order as
+        // the outputs (a column of ones), so the applied weights P/l sum to 1
+        // in this kernel's own f32 arithmetic.
+        l[i] = fmaf(pv[i], 1.0f, l[i]);
+      }
     }
   }
 
@@ -161,13 +160,16 @@ __global__ void __launch_bounds__(256) prefill_simt_kernel(SimtParams p) {
 
 cudaError_t launch_prefill_simt(const SimtParams& p, cudaStream_t s) {
   const size_t smem = 4 * 64 * kPad * sizeof(float);
-  static bool configured = false;
-  if (!configured) {
-    cudaError_t e = cudaFuncSetAttribute(prefill_simt_kernel,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         static_cast<int>(smem));
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  static bool configured[64] = {};  // the attribute is per device
+  if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+  if (!configured[dev]) {
+    e = cudaFuncSetAttribute(prefill_simt_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             static_cast<int>(smem));
     if (e != cudaSuccess) return e;
-    configured = true;
+    configured[dev] = true;
   }
   dim3 grid((p.Nq + kBM - 1) / kBM, p.B * p.H);
   prefill_simt_kernel<<<grid, 256, smem, s>>>(p);

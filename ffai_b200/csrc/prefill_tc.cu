@@ -11,22 +11,31 @@
 // query rows (two 128-row tiles, t = 0, 1) of one (sequence, head); both
 // tiles share every K/V block, so each block is fetched once for 256 rows.
 //
-//   warp 8      TMA producer: Q tiles, then a 3-stage ring of K/V blocks of
+//   warp 16     TMA producer: Q tiles, then a 3-stage ring of K/V blocks of
 //               128 keys (16 KB each, 128-byte swizzle).  Also owns TMEM.
-//   warp 9      MMA issuer (one thread):  S_t = Q_t K^T   (M=128, N=128, K=64)
+//   warps 17,18 MMA issuers, one thread per tile: S_t = Q_t K^T   (M=128, N=128, K=64)
 //                                         O_t += P_t V    (M=128, N=64,  K=128)
 //               with P_t read straight from tensor memory (the "A in TMEM"
-//               form), so probabilities never touch shared memory.
-//   warps 0-3   softmax for tile 0, warps 4-7 for tile 1: one thread per
-//               query row.  Each thread loads its row of S from TMEM, takes
-//               the block max, exponentiates in the log2 domain, keeps the
-//               row sum in f32 and writes bf16 P back over S.  The running
-//               max is only moved (and O rescaled in TMEM) when it grows by
-//               more than 2^8, so most blocks never touch O.  The last block
-//               is followed by the epilogue: O / sum to global memory.
+//               form), so probabilities never touch shared memory.  S_t(j+1)
+//               is issued as soon as the softmax has *read* S_t(j), before
+//               P_t(j).V, so the tensor core computes the next scores while
+//               the softmax of the current ones runs.
+//   warps 0-15  softmax, 8 warps per tile.  A warp owns 16 query rows, four
+//               lanes per row, each lane a quarter of the row's 128 keys (the
+//               16x256b TMEM access shape), so a row's max and sum reduce with
+//               two warp shuffles.  Each lane loads its scores, releases S,
+//               exponentiates in the log2 domain with packed f32x2 arithmetic
+//               -- 2 of every 8 pairs by a polynomial on the FMA pipe, the
+//               rest on MUFU --, sums the rounded probabilities it writes (so
+//               the applied weights P/l sum to 1) and stores bf16 P into its
+//               own TMEM buffer (16x128b shape, which lines up with the
+//               scores' layout).  The running max is only moved (and O
+//               rescaled in TMEM) when it grows by more than 2^8, so most
+//               blocks never touch O.  After the last block: O / l to global
+//               memory.
 //
-// Tensor memory (512 columns): S0 [0,128), S1 [128,256), O0 [256,320),
-// O1 [320,384).  P_t aliases the first 64 columns of S_t.
+// Tensor memory (512 columns): S0 [0,128), S1 [128,256), P0 [256,320),
+// P1 [320,384), O0 [384,448), O1 [448,512).
 //
 // Every wait is bounded (common.cuh); on a timeout the CTA raises an error
 // bit, drains its MMAs and TMA loads, frees TMEM and exits.
@@ -39,17 +48,21 @@ namespace {
 
 constexpr uint32_t kTileBytes = kTcRows * 64 * 2;  // 16 KB: 128 rows x 128 B
 constexpr uint32_t kTmemCols = 512;
-constexpr uint32_t kColS = 0, kColO = 256;
+constexpr uint32_t kColS = 0, kColP = 256, kColO = 384;  // + 128 t, + 64 t, + 64 t
+// Warps 0-15 softmax (warp w: tile w/8, TMEM lanes 32(w%4) + 16((w/4)%2) + [0,16)),
+// 16 the TMA producer, 17 and 18 the per-tile MMA issuers.
+constexpr int kWarpProducer = 16, kWarpMma0 = 17;
 
 struct __align__(8) TcBars {
   uint64_t q_full[2], q_empty[2];
   uint64_t k_full[kTcStages], v_full[kTcStages], kv_empty[kTcStages];
-  uint64_t s_full[2], p_full[2], o_done[2];
+  uint64_t s_full[2], sc_done[2], p_full[2], o_done[2];
   uint64_t drain;
   uint32_t tmem_base;
   int abort_flag;
 };
 
+// Q0, Q1, and the K and V rings, then the barriers.
 constexpr size_t kSmemTiles = (2 + 2 * kTcStages) * kTileBytes;
 constexpr size_t kSmemBytes = kSmemTiles + sizeof(TcBars) + 1024;  // +1024: alignment slack
 
@@ -152,15 +165,16 @@ __device__ __forceinline__ void run_producer(const CUtensorMap* tmQ, const CUten
 
 // ---------------------------------------------------------------- MMA issuer
 struct MmaState {
-  uint32_t kv_cnt;     // K/V blocks consumed (global over units)
   uint32_t q_use[2];   // Q tiles consumed per tile slot
-  uint32_t pv_cnt[2];  // PV groups issued per tile slot
-  uint32_t k_ready;    // kv_cnt value whose K stage has been waited for, +1
+  uint32_t s_cnt[2];   // S MMAs issued per tile slot
+  uint32_t pv_cnt[2];  // P.V groups issued per tile slot
+  uint32_t k_ready;    // (block index whose K stage has been waited for) + 1
 };
 
 template <int AB_F16>
-__device__ __forceinline__ bool issue_s(int t, bool first_of_unit, bool last_of_unit, uint32_t g, MmaState& st,
-                        uint8_t* sQ, uint8_t* sK, uint32_t tmem, TcBars* bars, unsigned* err) {
+__device__ __forceinline__ bool issue_s(int t, bool first_of_unit, bool last_of_unit, uint32_t g,
+                                        MmaState& st, uint8_t* sQ, uint8_t* sK, uint32_t tmem,
+                                        TcBars* bars, unsigned* err) {
   volatile int* abort_flag = &bars->abort_flag;
   const uint32_t s = g % kTcStages;
   if (st.k_ready != g + 1) {
@@ -172,9 +186,9 @@ __device__ __forceinline__ bool issue_s(int t, bool first_of_unit, bool last_of_
     if (!mbar_wait(&bars->q_full[t], st.q_use[t] & 1, abort_flag, err, kErrTimeoutMma)) return false;
     ++st.q_use[t];
   }
-  // S_t / P_t are about to be overwritten: the previous P_t.V must have read P_t.
-  if (st.pv_cnt[t] > 0 &&
-      !mbar_wait(&bars->o_done[t], (st.pv_cnt[t] - 1) & 1, abort_flag, err, kErrTimeoutMma))
+  // S_t is about to be overwritten: the softmax must have read the last one.
+  if (st.s_cnt[t] > 0 &&
+      !mbar_wait(&bars->sc_done[t], (st.s_cnt[t] - 1) & 1, abort_flag, err, kErrTimeoutMma))
     return false;
   tc_fence_after();
   constexpr uint32_t idesc = idesc_f16(AB_F16 ? 0u : 1u, kTcRows, kTcKeys, 0, 0);
@@ -184,13 +198,20 @@ __device__ __forceinline__ bool issue_s(int t, bool first_of_unit, bool last_of_
   for (int k = 0; k < 4; ++k)  // K = 64 = 4 x 16; +32 bytes per step inside the swizzle atom
     mma_ss(tmem + kColS + t * 128, dq + 2 * k, dk + 2 * k, idesc, k > 0 ? 1u : 0u);
   mma_commit(&bars->s_full[t]);
+  ++st.s_cnt[t];
   if (last_of_unit) mma_commit(&bars->q_empty[t]);
   return true;
 }
 
+// One MMA thread per Q tile, so the two tiles' chains (S -> softmax -> P.V)
+// advance independently; they meet only in the K/V ring, whose stages are
+// released when both threads have finished with them (kv_empty counts 2).
+// A thread whose tile is absent from a unit still walks that unit's blocks
+// and arrives on kv_empty for each, after waiting for the block's V, so its
+// arrivals can never run ahead into a later phase of the same stage.
 template <int AB_F16>
-__device__ __forceinline__ void run_mma(const TcParams& p, uint8_t* sQ, uint8_t* sK, uint8_t* sV, uint32_t tmem,
-                        TcBars* bars) {
+__device__ __forceinline__ void run_mma(const TcParams& p, int t, uint8_t* sQ, uint8_t* sK,
+                                        uint8_t* sV, uint32_t tmem, TcBars* bars) {
   volatile int* abort_flag = &bars->abort_flag;
   MmaState st{};
   int u = blockIdx.x;
@@ -200,9 +221,10 @@ __device__ __forceinline__ void run_mma(const TcParams& p, uint8_t* sQ, uint8_t*
   int cur_nblk = num_blocks(p, cur.seq);
   int j = 0;
   uint32_t g = 0;
-  for (int t = 0; t < cur.ntiles; ++t)
-    if (!issue_s<AB_F16>(t, true, cur_nblk == 1, g, st, sQ, sK, tmem, bars, p.err)) return;
+  if (t < cur.ntiles && !issue_s<AB_F16>(t, true, cur_nblk == 1, g, st, sQ, sK, tmem, bars, p.err))
+    return;
 
+  // P.V: M=128, N=64, A = P from TMEM, B = V MN-major (head dim contiguous).
   constexpr uint32_t idesc_pv = idesc_f16(AB_F16 ? 0u : 1u, kTcRows, 64, 0, 1);
   while (true) {
     // Next block in this CTA's flat sequence of (unit, key block).
@@ -219,29 +241,30 @@ __device__ __forceinline__ void run_mma(const TcParams& p, uint8_t* sQ, uint8_t*
         has_next = false;
       }
     }
+    // Scores of the next block first: they need only the softmax to have
+    // read the current ones, and run while it exponentiates them.
+    if (has_next && t < nxt.ntiles &&
+        !issue_s<AB_F16>(t, nxt_j == 0, nxt_j == nxt_nblk - 1, g + 1, st, sQ, sK, tmem, bars,
+                         p.err))
+      return;
     const uint32_t s = g % kTcStages;
     if (!mbar_wait(&bars->v_full[s], (g / kTcStages) & 1, abort_flag, p.err, kErrTimeoutMma)) return;
-    const uint64_t dv = smem_desc_sw128(smem_u32(sV + s * kTileBytes), 8192, 1024);
-    for (int t = 0; t < 2; ++t) {
-      if (t < cur.ntiles) {
-        if (!mbar_wait(&bars->p_full[t], st.pv_cnt[t] & 1, abort_flag, p.err, kErrTimeoutMma))
-          return;
-        tc_fence_after();
-        const uint32_t tp = tmem + kColS + t * 128;  // P_t: bf16 pairs in the first 64 columns
+    if (t < cur.ntiles) {
+      if (!mbar_wait(&bars->p_full[t], st.pv_cnt[t] & 1, abort_flag, p.err, kErrTimeoutMma))
+        return;
+      tc_fence_after();
+      const uint64_t dv = smem_desc_sw128(smem_u32(sV + s * kTileBytes), 8192, 1024);
+      const uint32_t tp = tmem + kColP + t * 64;  // P_t: bf16 pairs
 #pragma unroll
-        for (int k = 0; k < 8; ++k)  // 128 keys = 8 x 16; V advances 16 rows = 2048 B per step
-          mma_ts(tmem + kColO + t * 64, tp + k * 8, dv + k * (2048 >> 4), idesc_pv,
-                 (j > 0 || k > 0) ? 1u : 0u);
-        mma_commit(&bars->o_done[t]);
-        ++st.pv_cnt[t];
-      }
-      if (has_next && t < nxt.ntiles) {
-        if (!issue_s<AB_F16>(t, nxt_j == 0, nxt_j == nxt_nblk - 1, g + 1, st, sQ, sK, tmem, bars,
-                             p.err))
-          return;
-      }
+      for (int k = 0; k < 8; ++k)  // 128 keys = 8 x 16; V advances 16 rows = 2048 B per step
+        mma_ts(tmem + kColO + t * 64, tp + k * 8, dv + k * (2048 >> 4), idesc_pv,
+               (j > 0 || k > 0) ? 1u : 0u);
+      mma_commit(&bars->o_done[t]);
+      ++st.pv_cnt[t];
+      mma_commit(&bars->kv_empty[s]);
+    } else {
+      mbar_arrive(&bars->kv_empty[s]);
     }
-    mma_commit(&bars->kv_empty[s]);
     if (!has_next) break;
     if (nxt_j == 0) u += gridDim.x;
     cur = nxt;
@@ -252,51 +275,141 @@ __device__ __forceinline__ void run_mma(const TcParams& p, uint8_t* sQ, uint8_t*
 }
 
 // ---------------------------------------------------------------- softmax + epilogue
-__device__ __forceinline__ void store_row(const TcParams& p, const TcUnit& w, int row,
-                                          const float* o, float inv) {
-  if (p.out_bf16) {
-    __nv_bfloat16* dst;
-    if (p.out_token_major)
-      dst = static_cast<__nv_bfloat16*>(p.out) +
-            (static_cast<long long>(__ldg(p.q_start + w.seq) + row) * p.heads + w.head) * 64;
-    else
-      dst = static_cast<__nv_bfloat16*>(p.out) +
-            ((static_cast<long long>(w.seq) * p.heads + w.head) * p.out_rows + row) * 64;
-    uint4* d4 = reinterpret_cast<uint4*>(dst);
+// Store this thread's quarter of one output row, scaled by `inv`: head dims
+// 8k + 2 t0 and 8k + 2 t0 + 1 (k = 0..7) of row v of the 16x256b layout.
+__device__ __forceinline__ void store_row_quarter(const TcParams& p, const TcUnit& w, int row,
+                                                  int t0, const uint32_t (&o)[32], int v,
+                                                  float inv) {
+  long long base;
+  if (p.out_token_major)
+    base = (static_cast<long long>(__ldg(p.q_start + w.seq) + row) * p.heads + w.head) * 64;
+  else
+    base = ((static_cast<long long>(w.seq) * p.heads + w.head) * p.out_rows + row) * 64;
+  base += 2 * t0;
 #pragma unroll
-    for (int c = 0; c < 8; ++c) {
-      uint4 v;
-      v.x = pack_bf16x2(o[8 * c + 0] * inv, o[8 * c + 1] * inv);
-      v.y = pack_bf16x2(o[8 * c + 2] * inv, o[8 * c + 3] * inv);
-      v.z = pack_bf16x2(o[8 * c + 4] * inv, o[8 * c + 5] * inv);
-      v.w = pack_bf16x2(o[8 * c + 6] * inv, o[8 * c + 7] * inv);
-      d4[c] = v;
-    }
-  } else {
-    float* dst;
-    if (p.out_token_major)
-      dst = static_cast<float*>(p.out) +
-            (static_cast<long long>(__ldg(p.q_start + w.seq) + row) * p.heads + w.head) * 64;
+  for (int k = 0; k < 8; ++k) {
+    const float a = __uint_as_float(o[4 * k + 2 * v]) * inv;
+    const float b = __uint_as_float(o[4 * k + 2 * v + 1]) * inv;
+    if (p.out_bf16)
+      *reinterpret_cast<uint32_t*>(static_cast<__nv_bfloat16*>(p.out) + base + 8 * k) =
+          pack_bf16x2(a, b);
     else
-      dst = static_cast<float*>(p.out) +
-            ((static_cast<long long>(w.seq) * p.heads + w.head) * p.out_rows + row) * 64;
-    float4* d4 = reinterpret_cast<float4*>(dst);
-#pragma unroll
-    for (int c = 0; c < 16; ++c)
-      d4[c] = make_float4(o[4 * c] * inv, o[4 * c + 1] * inv, o[4 * c + 2] * inv,
-                          o[4 * c + 3] * inv);
+      *reinterpret_cast<float2*>(static_cast<float*>(p.out) + base + 8 * k) = make_float2(a, b);
   }
 }
 
+// Which pairs take the polynomial exp2 (FMA pipe) instead of MUFU ex2:
+// kPolyOf8 of every 8.  MUFU sustains 16 ex2 per clock per SM; moving a share
+// of the exponentials to the FMA pipe lets both run at once (measured best
+// at 2 of 8 on the long-form encoder workload).
+constexpr int kPolyOf8 = 2;
+
+// f32 += one 16-bit half of a packed pair, in one instruction.
 template <int AB_F16>
-__device__ __forceinline__ void run_softmax(const TcParams& p, int t, uint32_t tmem, TcBars* bars) {
+__device__ __forceinline__ float add_half_lo(float acc, uint32_t pk) {
+  if (AB_F16)
+    asm("{ .reg .b16 l, h;\n mov.b32 {l, h}, %1;\n add.rn.f32.f16 %0, l, %0;\n}"
+        : "+f"(acc) : "r"(pk));
+  else
+    asm("{ .reg .b16 l, h;\n mov.b32 {l, h}, %1;\n add.rn.f32.bf16 %0, l, %0;\n}"
+        : "+f"(acc) : "r"(pk));
+  return acc;
+}
+
+template <int AB_F16>
+__device__ __forceinline__ float add_half_hi(float acc, uint32_t pk) {
+  if (AB_F16)
+    asm("{ .reg .b16 l, h;\n mov.b32 {l, h}, %1;\n add.rn.f32.f16 %0, h, %0;\n}"
+        : "+f"(acc) : "r"(pk));
+  else
+    asm("{ .reg .b16 l, h;\n mov.b32 {l, h}, %1;\n add.rn.f32.bf16 %0, h, %0;\n}"
+        : "+f"(acc) : "r"(pk));
+  return acc;
+}
+
+// Exponentiate this thread's 64 raw scores of its two rows (v = 0, 1),
+// p = 2^(s * sl2 - m_v), and pack them into the 16-bit pairs the 16x128b
+// store writes: pk[2k + v] holds the keys 8k + 2 t0 and 8k + 2 t0 + 1 of row
+// v, i.e. P word 4k + t0.  Adds the rounded (packed) values to sum[v].
+//
+// m_v is integer-valued (the running max is kept as a ceiling), which lets the
+// polynomial path fold its range reduction into the score scaling:
+//   t = fma(s, sl2, 1.5*2^23 - m) = 1.5*2^23 + round(x)     (x = s*sl2 - m)
+//   f = fma(s, sl2, -(round(x) + m)) = x - round(x)           in [-0.5, 0.5]
+// both exact up to the single rounding of each FMA; 2^f by a degree-3
+// polynomial (this project's own minimax fit of 2^f on [-0.5, 0.5], max
+// relative error 7.5e-5) and round(x) spliced into the exponent field.
+// Clamping t at round(x) >= -125 keeps the splice in range; below that 2^x
+// < 2^-125 and the result is negligible whatever f is.
+template <int AB_F16, bool kTail>
+__device__ __forceinline__ void exp_pack_rows(const float* sf, float sl2, const float (&m)[2],
+                                              uint32_t (&pk)[32], float (&sum)[2]) {
+  const float kMagic = 12582912.0f;  // 1.5 * 2^23
+  const uint64_t c2 = f2_pack(sl2, sl2);
+  uint64_t n2[2], cm2[2];
+#pragma unroll
+  for (int v = 0; v < 2; ++v) {
+    const float neg = (m[v] == -INFINITY) ? 0.f : -m[v];
+    n2[v] = f2_pack(neg, neg);
+    cm2[v] = f2_pack(kMagic + neg, kMagic + neg);
+  }
+  const uint64_t kC3 = f2_pack(0.055171434f, 0.055171434f);
+  const uint64_t kC2 = f2_pack(0.24261081f, 0.24261081f);
+  const uint64_t kC1 = f2_pack(0.69326097f, 0.69326097f);
+  const uint64_t kC0 = f2_pack(0.99992812f, 0.99992812f);
+  float acc[2][2] = {{0.f, 0.f}, {0.f, 0.f}};
+#pragma unroll
+  for (int k = 0; k < 16; ++k) {
+#pragma unroll
+    for (int v = 0; v < 2; ++v) {
+      float p0, p1;
+      const uint64_t sv = f2_pack(sf[4 * k + 2 * v], sf[4 * k + 2 * v + 1]);
+      if (!kTail && (k % 8) < kPolyOf8) {
+        float t0, t1;
+        f2_unpack(f2_fma(sv, c2, cm2[v]), t0, t1);
+        t0 = fmaxf(t0, kMagic - 125.f);
+        t1 = fmaxf(t1, kMagic - 125.f);
+        const uint64_t t = f2_pack(t0, t1);
+        const uint64_t f = f2_fma(sv, c2, f2_sub(cm2[v], t));  // x - round(x)
+        uint64_t q = f2_fma(kC3, f, kC2);
+        q = f2_fma(q, f, kC1);
+        q = f2_fma(q, f, kC0);
+        float q0, q1;
+        f2_unpack(q, q0, q1);
+        // (bits(t) << 23) == round(x) << 23 modulo 2^32
+        p0 = __uint_as_float(__float_as_uint(q0) + (__float_as_uint(t0) << 23));
+        p1 = __uint_as_float(__float_as_uint(q1) + (__float_as_uint(t1) << 23));
+      } else {  // MUFU; masked columns are -inf and give exactly 0
+        float x0, x1;
+        f2_unpack(f2_fma(sv, c2, n2[v]), x0, x1);
+        p0 = ex2_approx(x0);
+        p1 = ex2_approx(x1);
+      }
+      const uint32_t w = AB_F16 ? pack_f16x2(p0, p1) : pack_bf16x2(p0, p1);
+      pk[2 * k + v] = w;
+      acc[v][k & 1] = add_half_hi<AB_F16>(add_half_lo<AB_F16>(acc[v][k & 1], w), w);
+    }
+  }
+  sum[0] = acc[0][0] + acc[0][1];
+  sum[1] = acc[1][0] + acc[1][1];
+}
+
+// Softmax warp w (0..15) serves tile t = w / 8, TMEM lanes [lb, lb + 16) with
+// lb = 32 (w % 4) + 16 ((w / 4) % 2): each lane quarter is reachable only from
+// warps with the same w % 4.  Thread (t0, t1) = (lane % 4, lane / 4) handles
+// rows lb + t1 and lb + t1 + 8, a quarter of each row's columns; the four
+// threads of a row reduce its max and sum with two shuffles.
+template <int AB_F16>
+__device__ __forceinline__ void run_softmax(const TcParams& p, uint32_t tmem, TcBars* bars) {
   volatile int* abort_flag = &bars->abort_flag;
   const int warp = threadIdx.x / 32;
   const int lane = threadIdx.x % 32;
-  const int quarter = warp % 4;  // TMEM lanes [32*quarter, 32*quarter+32)
-  const int r_in_tile = quarter * 32 + lane;
-  const uint32_t lane_addr = static_cast<uint32_t>(quarter * 32) << 16;
+  const int t = warp / 8;
+  const int lb = 32 * (warp % 4) + 16 * ((warp / 4) % 2);
+  const int t0 = lane & 3, t1 = lane >> 2;
+  const uint32_t lane_addr = static_cast<uint32_t>(lb) << 16;
   const uint32_t tS = tmem + lane_addr + kColS + t * 128;
+  const uint32_t tP = tmem + lane_addr + kColP + t * 64;
   const uint32_t tO = tmem + lane_addr + kColO + t * 64;
   const float sl2 = p.scale_log2;
   uint32_t s_cnt = 0, pv_cnt = 0;
@@ -307,86 +420,84 @@ __device__ __forceinline__ void run_softmax(const TcParams& p, int t, uint32_t t
     if (t >= w.ntiles) continue;
     const int kv_len = __ldg(p.k_len + w.seq);
     const int nblk = (kv_len + kTcKeys - 1) / kTcKeys;
-    float m_run = -INFINITY;  // running max, log2 domain, scaled
-    float l_run = 0.f;
+    float m_run[2] = {-INFINITY, -INFINITY};  // per row: log2 domain, integer-valued
+    float l_run[2] = {0.f, 0.f};              // per row: this thread's share of the sum
 
     for (int j = 0; j < nblk; ++j) {
       if (!warp_wait(&bars->s_full[t], s_cnt & 1, abort_flag, p.err, kErrTimeoutSoftmax)) return;
       ++s_cnt;
       tc_fence_after();
-      uint32_t sr[128];
-      tmem_ld32(tS + 0, *reinterpret_cast<uint32_t(*)[32]>(sr + 0));
-      tmem_ld32(tS + 32, *reinterpret_cast<uint32_t(*)[32]>(sr + 32));
-      tmem_ld32(tS + 64, *reinterpret_cast<uint32_t(*)[32]>(sr + 64));
-      tmem_ld32(tS + 96, *reinterpret_cast<uint32_t(*)[32]>(sr + 96));
+      uint32_t sr[64];
+      tmem_ld_16x256b_x16(tS, sr);
       tmem_wait_ld();
+      // S_t is in registers: the next block's scores may overwrite it.
+      tc_fence_before();
+      mbar_arrive(&bars->sc_done[t]);
       float* sf = reinterpret_cast<float*>(sr);
 
-      const int rem = kv_len - j * kTcKeys;
-      if (rem < kTcKeys) {
+      const int rem = kv_len - j * kTcKeys;  // valid keys in this block
+      const bool tail = rem < kTcKeys;
+      if (tail) {
 #pragma unroll
-        for (int c = 0; c < 128; ++c)
-          if (c >= rem) sf[c] = -INFINITY;
-      }
-      float mx0 = sf[0], mx1 = sf[1], mx2 = sf[2], mx3 = sf[3];
+        for (int k = 0; k < 16; ++k)
 #pragma unroll
-      for (int c = 4; c < 128; c += 4) {
-        mx0 = fmaxf(mx0, sf[c]);
-        mx1 = fmaxf(mx1, sf[c + 1]);
-        mx2 = fmaxf(mx2, sf[c + 2]);
-        mx3 = fmaxf(mx3, sf[c + 3]);
+          for (int x = 0; x < 2; ++x)
+            if (8 * k + 2 * t0 + x >= rem) sf[4 * k + x] = sf[4 * k + 2 + x] = -INFINITY;
       }
-      const float m_blk = fmaxf(fmaxf(mx0, mx1), fmaxf(mx2, mx3)) * sl2;
-      // Move the running max only when it grows by more than 8 (a factor of
-      // 256): P stays <= 256, exact in f32 sums and in bf16's exponent range.
-      const bool grow = m_blk > m_run + 8.0f;
-      float corr = 1.f;
-      if (grow) {
-        corr = ex2_approx(m_run - m_blk);  // 0 when m_run is -inf
-        m_run = m_blk;
-      }
-      const float neg = (m_run == -INFINITY) ? 0.f : -m_run;
-      float sum0 = 0.f, sum1 = 0.f, sum2 = 0.f, sum3 = 0.f;
-      uint32_t pk[64];
+      float mx[2];
 #pragma unroll
-      for (int c = 0; c < 64; c += 2) {
-        const float p0 = ex2_approx(fmaf(sf[2 * c + 0], sl2, neg));
-        const float p1 = ex2_approx(fmaf(sf[2 * c + 1], sl2, neg));
-        const float p2 = ex2_approx(fmaf(sf[2 * c + 2], sl2, neg));
-        const float p3 = ex2_approx(fmaf(sf[2 * c + 3], sl2, neg));
-        sum0 += p0;
-        sum1 += p1;
-        sum2 += p2;
-        sum3 += p3;
-        if (AB_F16) {
-          pk[c] = pack_f16x2(p0, p1);
-          pk[c + 1] = pack_f16x2(p2, p3);
-        } else {
-          pk[c] = pack_bf16x2(p0, p1);
-          pk[c + 1] = pack_bf16x2(p2, p3);
+      for (int v = 0; v < 2; ++v) {
+        float a = fmaxf(sf[2 * v], sf[2 * v + 1]), b = fmaxf(sf[4 + 2 * v], sf[4 + 2 * v + 1]);
+#pragma unroll
+        for (int k = 2; k < 16; k += 2) {
+          a = max3f(a, sf[4 * k + 2 * v], sf[4 * k + 2 * v + 1]);
+          b = max3f(b, sf[4 * k + 4 + 2 * v], sf[4 * k + 4 + 2 * v + 1]);
+        }
+        mx[v] = fmaxf(a, b);
+        mx[v] = fmaxf(mx[v], __shfl_xor_sync(0xffffffffu, mx[v], 1));
+        mx[v] = fmaxf(mx[v], __shfl_xor_sync(0xffffffffu, mx[v], 2));
+      }
+      // Move a row's running max only when it grows by more than 8 (a factor
+      // of 256): P stays <= 256, exact in f32 sums and in bf16's exponent
+      // range.  It is kept integer-valued, so corrections are exact powers of
+      // two and the polynomial exp2 can fold its range reduction into the
+      // scaling FMA.
+      float corr[2] = {1.f, 1.f};
+      bool grow_any = false;
+#pragma unroll
+      for (int v = 0; v < 2; ++v) {
+        const float m_blk = mx[v] * sl2;
+        if (m_blk > m_run[v] + 8.0f) {
+          const float m_new = ceilf(m_blk);
+          corr[v] = ex2_approx(m_run[v] - m_new);  // 0 when m_run is -inf
+          m_run[v] = m_new;
+          grow_any = true;
         }
       }
-      l_run = fmaf(l_run, corr, (sum0 + sum1) + (sum2 + sum3));
-      tmem_st32(tS + 0, *reinterpret_cast<uint32_t(*)[32]>(pk + 0));
-      tmem_st32(tS + 32, *reinterpret_cast<uint32_t(*)[32]>(pk + 32));
-      tmem_wait_st();
-      if (__any_sync(0xffffffffu, grow && j > 0)) {
-        // Rescale this warp's rows of O_t once the previous P.V has landed.
-        // Done after P is written, when the S registers are dead; the P
-        // arrive below still orders it before this block's P.V.
-        if (!warp_wait(&bars->o_done[t], (pv_cnt - 1) & 1, abort_flag, p.err, kErrTimeoutSoftmax))
-          return;
-        tc_fence_after();
-        uint32_t orr[64];
-        tmem_ld32(tO + 0, *reinterpret_cast<uint32_t(*)[32]>(orr + 0));
-        tmem_ld32(tO + 32, *reinterpret_cast<uint32_t(*)[32]>(orr + 32));
+      uint32_t pk[32];
+      float bsum[2];
+      if (tail)
+        exp_pack_rows<AB_F16, true>(sf, sl2, m_run, pk, bsum);
+      else
+        exp_pack_rows<AB_F16, false>(sf, sl2, m_run, pk, bsum);
+      l_run[0] = fmaf(l_run[0], corr[0], bsum[0]);
+      l_run[1] = fmaf(l_run[1], corr[1], bsum[1]);
+      // P_t and O_t are free once the previous P_t.V has completed.
+      if (pv_cnt > 0 &&
+          !warp_wait(&bars->o_done[t], (pv_cnt - 1) & 1, abort_flag, p.err, kErrTimeoutSoftmax))
+        return;
+      tc_fence_after();
+      if (__any_sync(0xffffffffu, grow_any && j > 0)) {
+        uint32_t orr[32];
+        tmem_ld_16x256b_x8(tO, orr);
         tmem_wait_ld();
 #pragma unroll
-        for (int c = 0; c < 64; ++c) orr[c] = __float_as_uint(__uint_as_float(orr[c]) * corr);
-        tmem_st32(tO + 0, *reinterpret_cast<uint32_t(*)[32]>(orr + 0));
-        tmem_st32(tO + 32, *reinterpret_cast<uint32_t(*)[32]>(orr + 32));
-        tmem_wait_st();
+        for (int c = 0; c < 32; ++c)
+          orr[c] = __float_as_uint(__uint_as_float(orr[c]) * corr[(c >> 1) & 1]);
+        tmem_st_16x256b_x8(tO, orr);
       }
+      tmem_st_16x128b_x16(tP, pk);
+      tmem_wait_st();
       tc_fence_before();
       mbar_arrive(&bars->p_full[t]);
       ++pv_cnt;
@@ -395,21 +506,25 @@ __device__ __forceinline__ void run_softmax(const TcParams& p, int t, uint32_t t
     // Epilogue: O_t / l to global memory.
     if (!warp_wait(&bars->o_done[t], (pv_cnt - 1) & 1, abort_flag, p.err, kErrTimeoutSoftmax)) return;
     tc_fence_after();
-    uint32_t orr[64];
-    tmem_ld32(tO + 0, *reinterpret_cast<uint32_t(*)[32]>(orr + 0));
-    tmem_ld32(tO + 32, *reinterpret_cast<uint32_t(*)[32]>(orr + 32));
+    uint32_t orr[32];
+    tmem_ld_16x256b_x8(tO, orr);
     tmem_wait_ld();
-    const int row = w.row0 + t * kTcRows + r_in_tile;
     const int q_len = __ldg(p.q_len + w.seq);
-    if (row < q_len) {
-      const float inv = 1.f / l_run;
-      store_row(p, w, row, reinterpret_cast<const float*>(orr), inv);
-      if (p.lse) {
-        const float lse = (m_run + __log2f(l_run)) * 0.69314718055994530942f;
-        if (p.out_token_major)
-          p.lse[static_cast<long long>(w.head) * p.lse_tokens + __ldg(p.q_start + w.seq) + row] = lse;
-        else
-          p.lse[(static_cast<long long>(w.seq) * p.heads + w.head) * p.out_rows + row] = lse;
+#pragma unroll
+    for (int v = 0; v < 2; ++v) {
+      float l = l_run[v];
+      l += __shfl_xor_sync(0xffffffffu, l, 1);
+      l += __shfl_xor_sync(0xffffffffu, l, 2);
+      const int row = w.row0 + t * kTcRows + lb + t1 + 8 * v;
+      if (row < q_len) {
+        store_row_quarter(p, w, row, t0, orr, v, 1.f / l);
+        if (p.lse && t0 == 0) {
+          const float lse = (m_run[v] + __log2f(l)) * 0.69314718055994530942f;
+          if (p.out_token_major)
+            p.lse[static_cast<long long>(w.head) * p.lse_tokens + __ldg(p.q_start + w.seq) + row] = lse;
+          else
+            p.lse[(static_cast<long long>(w.seq) * p.heads + w.head) * p.out_rows + row] = lse;
+        }
       }
     }
     // The next unit's first P.V overwrites O_t only after this thread's next
@@ -439,23 +554,24 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       mbar_init(&bars->q_full[t], 1);
       mbar_init(&bars->q_empty[t], 1);
       mbar_init(&bars->s_full[t], 1);
-      mbar_init(&bars->p_full[t], 128);
+      mbar_init(&bars->sc_done[t], 256);  // the tile's 8 softmax warps
+      mbar_init(&bars->p_full[t], 256);
       mbar_init(&bars->o_done[t], 1);
     }
     for (int s = 0; s < kTcStages; ++s) {
       mbar_init(&bars->k_full[s], 1);
       mbar_init(&bars->v_full[s], 1);
-      mbar_init(&bars->kv_empty[s], 1);
+      mbar_init(&bars->kv_empty[s], 2);  // one arrival per tile's MMA thread
     }
-    mbar_init(&bars->drain, 1);
+    mbar_init(&bars->drain, 2);
     bars->abort_flag = 0;
     fence_mbar_init();
   }
-  if (warp == 8) {
+  if (warp == kWarpProducer) {
     tmem_alloc(&bars->tmem_base, kTmemCols);
     tmem_relinquish();
   }
-  if (warp == 9 && lane == 0) {
+  if (warp == kWarpMma0 && lane == 0) {
     prefetch_tensormap(&tmQ);
     prefetch_tensormap(&tmK);
     prefetch_tensormap(&tmV);
@@ -465,24 +581,24 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   tc_fence_after();
   const uint32_t tmem = bars->tmem_base;
 
-  if (warp == 8) {
+  if (warp == kWarpProducer) {
     if (lane == 0) run_producer(&tmQ, &tmK, &tmV, p, sQ, sK, sV, bars);
-  } else if (warp == 9) {
+  } else if (warp == kWarpMma0 || warp == kWarpMma0 + 1) {
     if (lane == 0) {
-      run_mma<AB_F16>(p, sQ, sK, sV, tmem, bars);
-      // Wait for every MMA this thread issued before TMEM is released.
+      run_mma<AB_F16>(p, warp - kWarpMma0, sQ, sK, sV, tmem, bars);
+      // Wait for every MMA either thread issued before TMEM is released.
       int none = 0;
       mma_commit(&bars->drain);
       mbar_wait(&bars->drain, 0, &none, p.err, kErrTimeoutDrain);
     }
   } else {
-    run_softmax<AB_F16>(p, warp / 4, tmem, bars);
+    run_softmax<AB_F16>(p, tmem, bars);
   }
 
   __syncwarp();
   tc_fence_before();
   __syncthreads();
-  if (warp == 8) {
+  if (warp == kWarpProducer) {
     tc_fence_after();
     tmem_dealloc(tmem, kTmemCols);
   }

@@ -8,8 +8,8 @@ import pytest
 import torch
 
 from ffai_b200 import attention, workloads
-from helpers import (BF16_MAX_ABS, F32_REL, ROWSUM_TOL, assert_bf16_close, assert_f32_close,
-                     f32np, rowsum_error)
+from helpers import (LSE_TOL, ROWSUM_TOL, assert_bf16_close, assert_f32_close, f32np,
+                     rowsum_error)
 
 pytestmark = pytest.mark.gpu
 DEV = "cuda:0"
@@ -40,6 +40,17 @@ def test_decode_parity(oracle, keys, k_layout, dtype):
     B, H = q.shape[:2]
     err = rowsum_error(f32np(q).reshape(B * H, 1, 64), f32np(k).reshape(B * H, keys, 64), 1.0,
                        f32np(lse).reshape(B * H, 1))
+    assert err <= LSE_TOL, f"LSE off by {err:.2e}"
+
+
+@pytest.mark.parametrize("keys", [8, 448, 1500])
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
+def test_decode_rowsums(keys, dtype):
+    """Applied softmax weights sum to 1 within 1e-6 (V = ones)."""
+    q, k, _ = workloads.decode_inputs(keys, seed=8, dtype=dtype)
+    ones = torch.ones(k.shape, dtype=dtype)
+    out = attention.decode(q.to(DEV), k.to(DEV), ones.to(DEV))
+    err = (out.double() - 1.0).abs().max().item()
     assert err <= ROWSUM_TOL, f"row sums off by {err:.2e}"
 
 

@@ -10,8 +10,8 @@ import pytest
 import torch
 
 from ffai_b200 import attention, workloads
-from helpers import (ROWSUM_TOL, assert_bf16_close, assert_f32_close, f32np, oracle_encoder,
-                     rowsum_error)
+from helpers import (LSE_TC_TOL, LSE_TOL, ROWSUM_TOL, assert_bf16_close, assert_f32_close, f32np,
+                     oracle_encoder, rowsum_error)
 
 pytestmark = pytest.mark.gpu
 DEV = "cuda:0"
@@ -45,7 +45,7 @@ def test_tc_c2_base_encoder_batched(oracle):
     # row sums through the exported LSE, on a few (segment, head) pairs
     for b, h in [(0, 0), (3, 5), (7, 7)]:
         err = rowsum_error(f32np(q[b, h])[None], f32np(k[b, h])[None], S, f32np(lse[b, h])[None])
-        assert err <= ROWSUM_TOL, f"row sums off by {err:.2e} at ({b},{h})"
+        assert err <= LSE_TC_TOL, f"LSE off by {err:.2e} at ({b},{h})"
 
 
 def test_c1_tiny_encoder_f32(oracle):
@@ -72,7 +72,7 @@ def test_checked_f32_edges(oracle, N):
     assert_f32_close(f32np(out), ref, f"checked N={N}")
     err = rowsum_error(f32np(q).reshape(2, N, 64), f32np(k).reshape(2, N, 64), S,
                        f32np(lse).reshape(2, N))
-    assert err <= ROWSUM_TOL
+    assert err <= LSE_TOL
 
 
 def test_checked_causal_vs_f64(oracle):
@@ -131,7 +131,20 @@ def test_tc_lse_rowsums(oracle):
     _, lse = attention.prefill(q.to(DEV), k.to(DEV), v.to(DEV), scale=S, with_lse=True)
     err = rowsum_error(f32np(q).reshape(2, 1500, 64), f32np(k).reshape(2, 1500, 64), S,
                        f32np(lse).reshape(2, 1500))
-    assert err <= ROWSUM_TOL, f"row sums off by {err:.2e}"
+    assert err <= LSE_TC_TOL, f"LSE off by {err:.2e}"
+
+
+@pytest.mark.parametrize("path", ["tc_bf16", "tc_f16", "checked_f32"])
+def test_softmax_rowsums(path):
+    """Row sums of the applied softmax weights within 1e-6: with V = ones,
+    every output element is sum_j P_ij / l_i."""
+    dtype = {"tc_bf16": torch.bfloat16, "tc_f16": torch.float16, "checked_f32": torch.float32}[path]
+    q, k, _ = _inputs(2, 4, 1500, dtype=dtype, seed=55)
+    ones = torch.ones(2, 4, 1500, 64, dtype=dtype)
+    out = attention.prefill(q.to(DEV), k.to(DEV), ones.to(DEV), scale=S,
+                            checked=(path == "checked_f32"))
+    err = (out.double() - 1.0).abs().max().item()
+    assert err <= ROWSUM_TOL, f"{path}: row sums off by {err:.2e}"
 
 
 def test_tc_deterministic_and_no_stray_writes():
@@ -198,7 +211,7 @@ def test_varlen_small(oracle):
     a, b = cu[s], cu[s + 1]
     err = rowsum_error(f32np(q[a:b]).transpose(1, 0, 2), f32np(k[a:b]).transpose(1, 0, 2), S,
                        f32np(lse[:, a:b]))
-    assert err <= ROWSUM_TOL
+    assert err <= LSE_TC_TOL
 
 
 def test_varlen_c5_sampled(oracle):
