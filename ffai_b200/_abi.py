@@ -27,6 +27,7 @@ DT_F32, DT_BF16, DT_F16 = 0, 1, 2
 LAYOUT_HEADS_SPLIT, LAYOUT_TOKEN_MAJOR, LAYOUT_KT = 0, 1, 2
 # flags
 FLAG_CHECKED_F32 = 0x1
+FLAG_KV_STABLE = 0x2
 # ops
 OP_PREFILL, OP_DECODE, OP_VARLEN = 0, 1, 2
 

@@ -485,6 +485,32 @@ int decode_impl(ffai_attn_ctx* ctx, const ffai_attn_desc* d, const void* q, cons
   for (const void* ptr : {q, k, v, static_cast<const void*>(o)})
     if (reinterpret_cast<uintptr_t>(ptr) % 16 != 0)
       return set_error(ctx, FFAI_ATTN_ERR_INVALID, "decode operands must be 16-byte aligned");
+  if (num_splits == 0 && d->k_layout != FFAI_LAYOUT_KT &&
+      static_cast<long long>(rows) * kDecodeMaxCluster >= ctx->num_sms) {
+    // Row-major cache with enough rows to fill the GPU: the cluster kernel.
+    // Two CTAs per SM; each row split over S <= 8 CTAs of one cluster, with
+    // at least 16 keys per CTA.
+    int S = static_cast<int>(std::min<long long>(kDecodeMaxCluster, 2LL * ctx->num_sms / rows));
+    S = std::max(1, std::min(S, (kv + 15) / 16));
+    const int kpc = (kv + S - 1) / S;
+    DecodeParams p{};
+    p.q = q;
+    p.k = k;
+    p.v = v;
+    p.out = o;
+    p.lse = lse;
+    p.rows = rows;
+    p.kv_len = kv;
+    p.cap = cap;
+    p.q_dtype = d->q_dtype;
+    p.kv_dtype = d->kv_dtype;
+    p.out_dtype = d->out_dtype;
+    p.scale_log2 = d->scale * 1.4426950408889634f;
+    p.err = ctx->d_err;
+    p.kv_stable = (d->flags & FFAI_ATTN_FLAG_KV_STABLE) != 0;
+    FFAI_CUDA(ctx, launch_decode_cluster(p, S, kpc, s));
+    return FFAI_ATTN_OK;
+  }
   int chunk;
   if (num_splits > 0) {
     chunk = (kv + num_splits - 1) / num_splits;
@@ -512,6 +538,7 @@ int decode_impl(ffai_attn_ctx* ctx, const ffai_attn_desc* d, const void* q, cons
   p.out_dtype = d->out_dtype;
   p.k_kt = d->k_layout == FFAI_LAYOUT_KT;
   p.scale_log2 = d->scale * 1.4426950408889634f;
+  p.err = ctx->d_err;
   if (splits > 1) {
     int st = ensure(ctx, &ctx->d_part, &ctx->part_cap,
                     static_cast<size_t>(rows) * splits * kPartStride);

@@ -251,6 +251,262 @@ __global__ void __launch_bounds__(kDecThreads) decode_split_kernel(DecodeParams 
   }
 }
 
+// ---------------------------------------------------------------------------
+// Cluster decode for row-major caches (keys of 64 contiguous values).
+//
+// Row r is split into S contiguous key ranges, one per CTA of a thread-block
+// cluster of S CTAs (S <= 8), and the grid is rows x S CTAs with two CTAs
+// resident per SM, so a Whisper decode step (60-100 rows) fills every SM in a
+// single wave.  A producer lane copies the CTA's whole range into a ring of
+// shared-memory stages with 1-d bulk copies at kernel start (refilling the
+// ring only when a range is longer than the ring), so each SM has its share
+// of the cache in flight at once.  The eight consumer warps take disjoint
+// key slices of every stage and each keeps its own running (max, sum,
+// output): no block-wide barrier inside the key loop.  The warps' partials
+// merge once in shared memory, and the S CTAs' partials merge in the leader
+// CTA's shared memory over the cluster (distributed shared memory), so the
+// step needs no global workspace and no atomics.
+//
+// The kernel is launched as a programmatic dependent of the preceding kernel
+// on the stream: its CTAs are scheduled while that kernel drains and wait for
+// it (griddepcontrol.wait) before reading q; with kv_stable the producer
+// copies the cache before that wait.
+constexpr int kClWarps = 8;                        // consumer warps
+constexpr int kClThreads = (kClWarps + 1) * 32;    // + one producer warp
+constexpr int kClStages = 6;
+constexpr int kClSlot = 66;                        // m, l, o[64]
+
+template <typename T>
+struct ClCfg {
+  static constexpr int kKeys = 8192 / (64 * sizeof(T));  // keys per stage: 8 KB of K, 8 KB of V
+  static constexpr int kWarpKeys = kKeys / kClWarps;     // keys per warp per stage
+  static constexpr int kSteps = kWarpKeys / 4;           // 4 keys per warp-step
+  static constexpr size_t kSmem = 2ull * kClStages * kKeys * 64 * sizeof(T) +
+                                  2ull * kClStages * sizeof(uint64_t) +
+                                  2ull * kClWarps * kClSlot * sizeof(float) + 16;
+};
+
+// Eight consecutive cache values as f32 (16-bit caches: one 16-byte load).
+template <typename T>
+__device__ __forceinline__ void load8_f32(const T* src, float (&x)[8]) {
+  if constexpr (sizeof(T) == 4) {
+    const float4 a = *reinterpret_cast<const float4*>(src);
+    const float4 b = *reinterpret_cast<const float4*>(src + 4);
+    x[0] = a.x; x[1] = a.y; x[2] = a.z; x[3] = a.w;
+    x[4] = b.x; x[5] = b.y; x[6] = b.z; x[7] = b.w;
+  } else {
+    const uint4 w = *reinterpret_cast<const uint4*>(src);
+    const uint32_t u[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      if constexpr (std::is_same<T, __nv_bfloat16>::value) {
+        x[2 * i] = __uint_as_float(u[i] << 16);
+        x[2 * i + 1] = __uint_as_float(u[i] & 0xffff0000u);
+      } else {
+        const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&u[i]));
+        x[2 * i] = f.x;
+        x[2 * i + 1] = f.y;
+      }
+    }
+  }
+}
+
+template <typename T>
+__global__ void __launch_bounds__(kClThreads, 2) decode_cluster_kernel(DecodeParams p, int S,
+                                                                        int kpc) {
+  using Cfg = ClCfg<T>;
+  constexpr int KS = Cfg::kKeys;
+  extern __shared__ __align__(128) uint8_t dsm[];
+  T* kbuf = reinterpret_cast<T*>(dsm);
+  T* vbuf = kbuf + kClStages * KS * 64;
+  uint64_t* full = reinterpret_cast<uint64_t*>(vbuf + kClStages * KS * 64);
+  uint64_t* empty = full + kClStages;
+  float* wslot = reinterpret_cast<float*>(empty + kClStages);  // [8][66] per-warp partials
+  float* cslot = wslot + kClWarps * kClSlot;                   // [8][66] per-CTA partials (leader)
+  __shared__ int s_abort;
+
+  const int tid = threadIdx.x, warp = tid / 32, lane = tid % 32;
+  const int rank = S > 1 ? static_cast<int>(cluster_ctarank()) : 0;
+  const int row = blockIdx.x / S;
+  const int k0 = min(p.kv_len, rank * kpc);
+  const int k1 = min(p.kv_len, k0 + kpc);
+  const int nch = (k1 - k0 + KS - 1) / KS;
+  if (S > 1) cluster_arrive_relaxed();  // paired with the wait before the merge
+  griddep_launch_dependents();
+
+  if (tid == 0) {
+    for (int i = 0; i < kClStages; ++i) {
+      mbar_init(&full[i], 1);
+      mbar_init(&empty[i], kClWarps);
+    }
+    s_abort = 0;
+    fence_mbar_init();
+  }
+  __syncthreads();
+
+  const size_t base = (static_cast<size_t>(row) * p.cap + k0) * 64;
+  if (warp == kClWarps) {
+    // Producer: all of the range's stages at once, then refills as warps free them.
+    if (!p.kv_stable) griddep_wait();
+    if (lane == 0) {
+      int issued = 0;
+      for (int c = 0; c < nch; ++c) {
+        const int st = c % kClStages;
+        if (c >= kClStages &&
+            !mbar_wait(&empty[st], ((c / kClStages) - 1) & 1, &s_abort, p.err, kErrTimeoutProducer))
+          break;
+        const int n = min(KS, k1 - k0 - c * KS);
+        const uint32_t bytes = static_cast<uint32_t>(n) * 64 * sizeof(T);
+        mbar_arrive_expect_tx(&full[st], 2 * bytes);
+        bulk_load(kbuf + st * KS * 64, static_cast<const T*>(p.k) + base + c * KS * 64, bytes,
+                  &full[st]);
+        bulk_load(vbuf + st * KS * 64, static_cast<const T*>(p.v) + base + c * KS * 64, bytes,
+                  &full[st]);
+        ++issued;
+      }
+      if (s_abort) {
+        // Wait (bounded, ignoring the abort flag) for the last armed phase of
+        // every stage so no copy lands after the CTA has exited.
+        int none = 0;
+        for (int i = 0; i < kClStages && i < issued; ++i) {
+          const int arms = (issued - 1 - i) / kClStages + 1;
+          mbar_wait(&full[i], (arms - 1) & 1, &none, p.err, kErrTimeoutDrain);
+        }
+      }
+    }
+    __syncwarp();
+  } else {
+    // Consumer warp: lanes 8g..8g+7 hold key g of each 4-key step, 8 head
+    // dims each (part); the running max m is warp-uniform.
+    const int kin = lane / 8, part = lane % 8;
+    griddep_wait();  // q (and the output buffers) belong to the preceding kernels
+    float qv[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e)
+      qv[e] = load_q(p.q, p.q_dtype, static_cast<size_t>(row) * 64 + part * 8 + e) * p.scale_log2;
+    float m = -INFINITY, l = 0.f, o[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) o[e] = 0.f;
+    for (int c = 0; c < nch; ++c) {
+      const int st = c % kClStages;
+      if (!mbar_wait(&full[st], (c / kClStages) & 1, &s_abort, p.err, kErrTimeoutConsumer)) break;
+      const int n = min(KS, k1 - k0 - c * KS);
+      const T* ks = kbuf + st * KS * 64;
+      const T* vs = vbuf + st * KS * 64;
+      float sc[Cfg::kSteps];
+      float mx = -INFINITY;
+#pragma unroll
+      for (int i = 0; i < Cfg::kSteps; ++i) {
+        const int key = warp * Cfg::kWarpKeys + i * 4 + kin;
+        float a = 0.f;
+        if (key < n) {
+          float x[8];
+          load8_f32(ks + key * 64 + part * 8, x);
+#pragma unroll
+          for (int e = 0; e < 8; ++e) a = fmaf(qv[e], x[e], a);
+        }
+        a += __shfl_xor_sync(0xffffffffu, a, 1);
+        a += __shfl_xor_sync(0xffffffffu, a, 2);
+        a += __shfl_xor_sync(0xffffffffu, a, 4);
+        sc[i] = key < n ? a : -INFINITY;
+        mx = fmaxf(mx, sc[i]);
+      }
+      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 8));
+      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16));
+      if (mx > m) {  // warp-uniform
+        const float corr = m == -INFINITY ? 0.f : exp2f(m - mx);
+        m = mx;
+        l *= corr;
+#pragma unroll
+        for (int e = 0; e < 8; ++e) o[e] *= corr;
+      }
+#pragma unroll
+      for (int i = 0; i < Cfg::kSteps; ++i) {
+        const int key = warp * Cfg::kWarpKeys + i * 4 + kin;
+        if (key < n) {
+          const float pj = exp2f(sc[i] - m);
+          l += pj;
+          float x[8];
+          load8_f32(vs + key * 64 + part * 8, x);
+#pragma unroll
+          for (int e = 0; e < 8; ++e) o[e] = fmaf(pj, x[e], o[e]);
+        }
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty[st]);
+    }
+    // Sum the four key groups; lanes 0-7 then hold the warp's o[64].
+    l += __shfl_xor_sync(0xffffffffu, l, 8);
+    l += __shfl_xor_sync(0xffffffffu, l, 16);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      o[e] += __shfl_xor_sync(0xffffffffu, o[e], 8);
+      o[e] += __shfl_xor_sync(0xffffffffu, o[e], 16);
+    }
+    float* ws = wslot + warp * kClSlot;
+    if (lane < 8) {
+#pragma unroll
+      for (int e = 0; e < 8; ++e) ws[2 + lane * 8 + e] = o[e];
+    }
+    if (lane == 0) {
+      ws[0] = m;
+      ws[1] = l;
+    }
+  }
+  __syncthreads();
+
+  // CTA partial over the eight warps (threads 0-63: one head dim each).
+  float M = -INFINITY, L = 0.f, O = 0.f;
+  if (tid < 64) {
+#pragma unroll
+    for (int w = 0; w < kClWarps; ++w) M = fmaxf(M, wslot[w * kClSlot]);
+#pragma unroll
+    for (int w = 0; w < kClWarps; ++w) {
+      const float mw = wslot[w * kClSlot];
+      const float f = mw == -INFINITY ? 0.f : exp2f(mw - M);
+      L = fmaf(wslot[w * kClSlot + 1], f, L);
+      O = fmaf(wslot[w * kClSlot + 2 + tid], f, O);
+    }
+  }
+  if (S > 1) {
+    __syncwarp();
+    cluster_wait();  // every CTA of the cluster has started: its shared memory is mapped
+    if (tid < 64) {
+      const uint32_t dst = mapa_shared(smem_u32(cslot + rank * kClSlot), 0);
+      st_cluster_f32(dst + 4u * (2 + tid), O);
+      if (tid == 0) {
+        st_cluster_f32(dst, M);
+        st_cluster_f32(dst + 4u, L);
+      }
+    }
+    __syncwarp();
+    cluster_arrive();
+    cluster_wait();
+    if (rank != 0) return;
+    if (tid < 64) {
+      M = -INFINITY;
+      for (int c = 0; c < S; ++c) M = fmaxf(M, cslot[c * kClSlot]);
+      L = 0.f;
+      O = 0.f;
+      for (int c = 0; c < S; ++c) {
+        const float mc = cslot[c * kClSlot];
+        const float f = mc == -INFINITY ? 0.f : exp2f(mc - M);
+        L = fmaf(cslot[c * kClSlot + 1], f, L);
+        O = fmaf(cslot[c * kClSlot + 2 + tid], f, O);
+      }
+    }
+  }
+  if (tid < 64) {
+    const float val = O / L;
+    if (p.out_dtype == 0)
+      static_cast<float*>(p.out)[static_cast<size_t>(row) * 64 + tid] = val;
+    else
+      static_cast<__nv_bfloat16*>(p.out)[static_cast<size_t>(row) * 64 + tid] =
+          __float2bfloat16(val);
+    if (tid == 0 && p.lse) p.lse[row] = (M + log2f(L)) * 0.69314718055994530942f;
+  }
+}
+
 template <typename T, int CH>
 cudaError_t launch_t(const DecodeParams& p, cudaStream_t s) {
   dim3 grid(p.splits, p.rows);
@@ -267,7 +523,54 @@ cudaError_t launch_ch(const DecodeParams& p, cudaStream_t s) {
   return launch_t<T, 128>(p, s);
 }
 
+template <typename T>
+cudaError_t launch_cluster_t(const DecodeParams& p, int S, int kpc, cudaStream_t s) {
+  const size_t smem = ClCfg<T>::kSmem;
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  static bool configured[64] = {};
+  if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+  if (!configured[dev]) {
+    e = cudaFuncSetAttribute(decode_cluster_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             static_cast<int>(smem));
+    if (e != cudaSuccess) return e;
+    configured[dev] = true;
+  }
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3(static_cast<unsigned>(p.rows) * S);
+  cfg.blockDim = dim3(kClThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = S;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 2;
+  e = cudaLaunchKernelEx(&cfg, decode_cluster_kernel<T>, p, S, kpc);
+  if (e != cudaSuccess) return e;
+  return cudaGetLastError();
+}
+
 }  // namespace
+
+cudaError_t launch_decode_cluster(const DecodeParams& p, int splits, int keys_per_cta,
+                                  cudaStream_t s) {
+  if (splits < 1 || splits > kDecodeMaxCluster) return cudaErrorInvalidValue;
+  switch (p.kv_dtype) {
+    case 0:
+      return launch_cluster_t<float>(p, splits, keys_per_cta, s);
+    case 1:
+      return launch_cluster_t<__nv_bfloat16>(p, splits, keys_per_cta, s);
+    case 2:
+      return launch_cluster_t<__half>(p, splits, keys_per_cta, s);
+  }
+  return cudaErrorInvalidValue;
+}
 
 cudaError_t launch_decode(const DecodeParams& p, cudaStream_t s) {
   switch (p.kv_dtype) {

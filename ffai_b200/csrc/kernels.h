@@ -28,9 +28,19 @@ struct DecodeParams {
   int q_dtype, kv_dtype, out_dtype;
   int k_kt;
   float scale_log2;
+  unsigned* err;  // device error word (bounded waits of the cluster kernel)
+  int kv_stable;  // cluster kernel: copy K/V before the programmatic-dependency wait
 };
 
 cudaError_t launch_decode(const DecodeParams& p, cudaStream_t s);
+
+// Cluster variant for row-major K (heads-split caches): p.rows x `splits`
+// CTAs, each row's keys split into ranges of `keys_per_cta` over one cluster
+// of `splits` CTAs (1..kDecodeMaxCluster) that merge through distributed
+// shared memory.  Uses no workspace (p.part, p.counters, p.chunk ignored).
+constexpr int kDecodeMaxCluster = 8;
+cudaError_t launch_decode_cluster(const DecodeParams& p, int splits, int keys_per_cta,
+                                  cudaStream_t s);
 
 // ---- checked f32 prefill (prefill_simt.cu) ---------------------------------
 

@@ -24,9 +24,9 @@
 //               lanes per row, each lane a quarter of the row's 128 keys (the
 //               16x256b TMEM access shape), so a row's max and sum reduce with
 //               two warp shuffles.  Each lane loads its scores, releases S,
-//               exponentiates in the log2 domain with packed f32x2 arithmetic
-//               -- 2 of every 8 pairs by a polynomial on the FMA pipe, the
-//               rest on MUFU --, sums the rounded probabilities it writes (so
+//               exponentiates in the log2 domain (packed f32x2 scaling, MUFU
+//               ex2; a polynomial exp2 on the FMA pipe can take a share of
+//               the pairs), sums the rounded probabilities it writes (so
 //               the applied weights P/l sum to 1) and stores bf16 P into its
 //               own TMEM buffer (16x128b shape, which lines up with the
 //               scores' layout).  The running max is only moved (and O
@@ -299,10 +299,11 @@ __device__ __forceinline__ void store_row_quarter(const TcParams& p, const TcUni
 }
 
 // Which pairs take the polynomial exp2 (FMA pipe) instead of MUFU ex2:
-// kPolyOf8 of every 8.  MUFU sustains 16 ex2 per clock per SM; moving a share
-// of the exponentials to the FMA pipe lets both run at once (measured best
-// at 2 of 8 on the long-form encoder workload).
-constexpr int kPolyOf8 = 2;
+// kPolyOf8 of every 8.  MUFU sustains 16 ex2 per clock per SM; the
+// polynomial costs about ten issue slots per element, and with the softmax
+// issue-bound the measured best on the long-form encoder workload is 0 (the
+// path stays available for a kernel whose MUFU is the tighter limit).
+constexpr int kPolyOf8 = 0;
 
 // f32 += one 16-bit half of a packed pair, in one instruction.
 template <int AB_F16>

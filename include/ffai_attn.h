@@ -62,6 +62,14 @@ extern "C" {
 /* Run the f32 SIMT kernel (f32 operands only) instead of the bf16 tensor-core
  * kernel: max relative error 1e-5 instead of the bf16 path's 1e-2 abs. */
 #define FFAI_ATTN_FLAG_CHECKED_F32 0x1u
+/* Decode only: the K/V cache is not written by work queued earlier on the
+ * same stream.  The decode kernel is always launched as a programmatic
+ * dependent (it waits for the preceding kernel before reading q); with this
+ * flag it also starts copying the cache before that wait, overlapping the
+ * preceding kernel's tail.  True for cross-attention caches (written once per
+ * utterance); false for a self-attention cache whose newest key the
+ * preceding kernel appends.  No reference counterpart. */
+#define FFAI_ATTN_FLAG_KV_STABLE 0x2u
 
 /* ---- operations, for ffai_attn_check ---- */
 #define FFAI_OP_PREFILL 0

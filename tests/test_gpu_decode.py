@@ -116,3 +116,42 @@ def test_decode_beams_independent():
     keep = [0, 1, 3, 4]
     assert torch.equal(a[keep], b[keep])
     assert not torch.equal(a[2], b[2])
+
+
+@pytest.mark.parametrize("keys", [15, 16, 17, 63, 64, 65, 383, 384, 385, 769, 5000])
+@pytest.mark.parametrize("beams,heads", [(5, 12), (1, 20), (2, 8), (16, 20)])
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
+def test_decode_row_and_key_counts(oracle, keys, beams, heads, dtype):
+    """Ragged key counts around the stage and split boundaries, for row counts
+    that take the cluster kernel (>= 19 rows on 148 SMs) and the split kernel."""
+    q, k, v = workloads.decode_inputs(keys, seed=9, dtype=dtype, beams=beams, heads=heads)
+    ref = _oracle_decode(oracle, q, k, v, scale=0.125)
+    out = attention.decode(q.to(DEV), k.to(DEV), v.to(DEV), scale=0.125)
+    assert_f32_close(f32np(out), ref, f"keys={keys} rows={beams * heads} {dtype}")
+
+
+def test_decode_reads_q_written_just_before(oracle):
+    """The decode kernel starts while the preceding kernel drains; it must
+    still see the q that kernel wrote (no host sync between the launches)."""
+    caches = [workloads.decode_inputs(1500, seed=20 + i) for i in range(4)]
+    qbuf = torch.zeros(5, 12, 1, 64, device=DEV)
+    k = caches[0][1].to(DEV)
+    v = caches[0][2].to(DEV)
+    qs = [c[0].to(DEV) for c in caches]
+    outs = []
+    for i in range(4):
+        qbuf.copy_(qs[i])          # a kernel on the same stream
+        qbuf.mul_(1.0)             # and a second one right before the decode
+        outs.append(attention.decode(qbuf, k, v, kv_stable=(i % 2 == 1)))
+    torch.cuda.synchronize()
+    for i in range(4):
+        ref = _oracle_decode(oracle, caches[i][0], caches[0][1], caches[0][2])
+        assert_f32_close(f32np(outs[i]), ref, f"q written before decode {i}")
+
+
+def test_decode_kv_stable_same_bits():
+    q, k, v = workloads.decode_inputs(1500, seed=21)
+    qd, kd, vd = q.to(DEV), k.to(DEV), v.to(DEV)
+    a = attention.decode(qd, kd, vd).clone()
+    b = attention.decode(qd, kd, vd, kv_stable=True)
+    assert torch.equal(a, b)
