@@ -127,59 +127,6 @@ class ClockSampler:
 
 
 # ----------------------------------------------------------------- distributed
-class Dist:
-    def __init__(self):
-        self.world = int(os.environ.get("WORLD_SIZE", "1"))
-        self.rank = int(os.environ.get("RANK", "0"))
-        self.local = int(os.environ.get("LOCAL_RANK", "0"))
-        self.pg = False
-
-    def init(self):
-        import torch
-        torch.cuda.set_device(self.local)
-        if self.world > 1:
-            import torch.distributed as dist
-            dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=180),
-                                    device_id=torch.device("cuda", self.local))
-            self.pg = True
-
-    def barrier(self):
-        if self.pg:
-            import torch.distributed as dist
-            dist.barrier(device_ids=[self.local])
-
-    def max(self, x: float) -> float:
-        if not self.pg:
-            return x
-        import torch
-        import torch.distributed as dist
-        t = torch.tensor([x], dtype=torch.float64, device=f"cuda:{self.local}")
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        return float(t.item())
-
-    def sum(self, x: float) -> float:
-        if not self.pg:
-            return x
-        import torch
-        import torch.distributed as dist
-        t = torch.tensor([x], dtype=torch.float64, device=f"cuda:{self.local}")
-        dist.all_reduce(t, op=dist.ReduceOp.SUM)
-        return float(t.item())
-
-    def gather_objects(self, obj):
-        if not self.pg:
-            return [obj]
-        import torch.distributed as dist
-        out = [None] * self.world
-        dist.all_gather_object(out, obj)
-        return out
-
-    def close(self):
-        if self.pg:
-            import torch.distributed as dist
-            dist.destroy_process_group()
-
-
 def timed(dist, steps, fn):
     """Barrier + sync, K steps between CUDA events, sync + barrier; max over ranks (s)."""
     import torch
@@ -413,11 +360,7 @@ def run_ours(args, dist):
         if dist.world > 1:
             run_id = os.environ.get("TORCHELASTIC_RUN_ID", os.environ.get("MASTER_PORT", "x"))
             name = f"ffai_bench_out_{run_id}"
-            if dist.rank == 0:
-                shared = partition.SharedHostBuffer(name, out_bytes, create=True)
-            dist.barrier()
-            if dist.rank != 0:
-                shared = partition.SharedHostBuffer(name, out_bytes, create=False)
+            shared = partition.open_shared_output(dist, name, out_bytes)
             pinned = shared.pin()
             raw = torch.frombuffer(shared.map, dtype=torch.bfloat16, count=out_bytes // 2)
             host_out = raw.view(cfg.segments, cfg.heads, cfg.seq, 64)[lo:hi]
@@ -436,13 +379,10 @@ def run_ours(args, dist):
         e_steps = max(1, min(args.steps, 10))
         # checksum of checksums: each rank's slice of the shared output equals
         # its device result; rank 0 checks the gathered whole.
-        mine = partition.checksum(inputs[0][3].view(torch.int16).cpu().numpy())
-        sums = dist.gather_objects(mine)
-        gather_ok = None
-        if dist.rank == 0:
-            whole = raw if dist.world > 1 else host_out.reshape(-1)
-            gather_ok = partition.checksum(whole.view(torch.int16).numpy()) == (
-                sum(sums) % 2**64)
+        whole = (raw if dist.world > 1 else host_out.reshape(-1)) if dist.rank == 0 else None
+        gather_ok = partition.gather_verified(
+            dist, inputs[0][3].view(torch.int16).cpu().numpy(),
+            whole.view(torch.int16).numpy() if whole is not None else None)
         e2e = {"value": round(flops_job * e_steps / e_max / 1e12, 3), "unit": "TFLOP/s",
                "h2d_bytes_per_step": int(3 * cfg.segments * seg_bytes),
                "d2h_bytes_per_step": int(out_bytes),
@@ -508,7 +448,8 @@ def main():
     ap.add_argument("--segments", type=int, default=0,
                     help="profiling only: run a smaller batch of c4 segments")
     args = ap.parse_args()
-    dist = Dist()
+    from ffai_b200.partition import RankGroup
+    dist = RankGroup("nccl")
     if args.impl == "reference":
         run_reference(args, dist)
         return

@@ -13,6 +13,7 @@ B200 build spreads segment batches over the 8 GPUs of one box.
 
 from __future__ import annotations
 
+import datetime
 import heapq
 import mmap
 import os
@@ -115,6 +116,105 @@ class SharedHostBuffer:
                 os.unlink(self.path)
             except FileNotFoundError:
                 pass
+
+
+class RankGroup:
+    """The ranks of one node, one process per GPU, as a launcher (torchrun)
+    describes them in RANK / LOCAL_RANK / WORLD_SIZE / MASTER_*.
+
+    The process group carries only control traffic: barriers, the max over
+    ranks of a device time, sums of counters and a gather of small objects
+    (checksums).  No tensor of the path crosses it.  `backend` is "nccl" on
+    the GPU box (control tensors on the rank's GPU) or "gloo" (CPU tensors),
+    which the CPU tests use.
+    """
+
+    def __init__(self, backend: str = "nccl", timeout_s: float = 180.0):
+        self.world = int(os.environ.get("WORLD_SIZE", "1"))
+        self.rank = int(os.environ.get("RANK", "0"))
+        self.local = int(os.environ.get("LOCAL_RANK", "0"))
+        self.backend = backend
+        self.timeout_s = timeout_s
+        self.pg = False
+
+    def _device(self):
+        import torch
+        return torch.device("cuda", self.local) if self.backend == "nccl" else torch.device("cpu")
+
+    def init(self):
+        import torch
+        if self.backend == "nccl":
+            torch.cuda.set_device(self.local)
+        if self.world > 1:
+            import torch.distributed as dist
+            kw = {"device_id": self._device()} if self.backend == "nccl" else {}
+            dist.init_process_group(self.backend,
+                                    timeout=datetime.timedelta(seconds=self.timeout_s), **kw)
+            self.pg = True
+        return self
+
+    def barrier(self):
+        if self.pg:
+            import torch.distributed as dist
+            if self.backend == "nccl":
+                dist.barrier(device_ids=[self.local])
+            else:
+                dist.barrier()
+
+    def _reduce(self, x: float, op) -> float:
+        import torch
+        import torch.distributed as dist
+        t = torch.tensor([x], dtype=torch.float64, device=self._device())
+        dist.all_reduce(t, op=op)
+        return float(t.item())
+
+    def max(self, x: float) -> float:
+        if not self.pg:
+            return x
+        import torch.distributed as dist
+        return self._reduce(x, dist.ReduceOp.MAX)
+
+    def sum(self, x: float) -> float:
+        if not self.pg:
+            return x
+        import torch.distributed as dist
+        return self._reduce(x, dist.ReduceOp.SUM)
+
+    def gather_objects(self, obj):
+        if not self.pg:
+            return [obj]
+        import torch.distributed as dist
+        out = [None] * self.world
+        dist.all_gather_object(out, obj)
+        return out
+
+    def close(self):
+        if self.pg:
+            import torch.distributed as dist
+            dist.destroy_process_group()
+            self.pg = False
+
+
+def open_shared_output(group: RankGroup, name: str, nbytes: int) -> SharedHostBuffer:
+    """The node's host output buffer: rank 0 creates it, the others attach
+    after a barrier.  Every rank then writes only its own slice."""
+    buf = None
+    if group.rank == 0:
+        buf = SharedHostBuffer(name, nbytes, create=True)
+    group.barrier()
+    if group.rank != 0:
+        buf = SharedHostBuffer(name, nbytes, create=False)
+    return buf
+
+
+def gather_verified(group: RankGroup, local_slice: np.ndarray, whole: np.ndarray | None):
+    """Checksum of checksums: every rank reports the checksum of the result it
+    computed; rank 0 compares their sum with the checksum of the gathered
+    buffer.  Returns True/False on rank 0, None elsewhere."""
+    sums = group.gather_objects(checksum(local_slice))
+    if group.rank != 0:
+        return None
+    return checksum(whole) == sum(sums) % 2**64
 
 
 def checksum(a: np.ndarray) -> int:

@@ -146,6 +146,8 @@ def flash_head(q, kt, v, out_stride=HD) -> np.ndarray:
     """One head: q (seq,64) pre-scaled, kt (64,seq), v (seq,64) -> (seq,64)."""
     q, kt, v = _f32(q), _f32(kt), _f32(v)
     seq = q.shape[0]
+    if q.shape != (seq, HD) or kt.shape != (HD, seq) or v.shape != (seq, HD) or out_stride < HD:
+        raise ValueError(f"flash_head shapes q {q.shape} kt {kt.shape} v {v.shape}")
     out = np.zeros((seq, out_stride), np.float32)
     lib().ora_flash_head_strided(_p(q), _p(kt), _p(v), _p(out), seq, out_stride)
     return out[:, :HD] if out_stride != HD else out
@@ -154,7 +156,11 @@ def flash_head(q, kt, v, out_stride=HD) -> np.ndarray:
 def flash_units(q, kt, v, threads=None) -> np.ndarray:
     """Many heads (units, seq, 64) with kt (units, 64, seq), on host threads."""
     q, kt, v = _f32(q), _f32(kt), _f32(v)
+    if q.ndim != 3 or q.shape[2] != 64:
+        raise ValueError(f"q must be (units, seq, 64), got {q.shape}")
     units, seq = q.shape[0], q.shape[1]
+    if kt.shape != (units, 64, seq) or v.shape != (units, seq, 64):
+        raise ValueError(f"kt {kt.shape} / v {v.shape} do not match q {q.shape}")
     out = np.empty_like(q)
     lib().ora_flash_units(_p(q), _p(kt), _p(v), _p(out), units, seq,
                           threads or default_threads())
@@ -177,6 +183,8 @@ def xattn_rows(q, kt, v, threads=1) -> np.ndarray:
     """Decode rows: q (rows,64), kt (rows,64,keys), v (rows,keys,64), f32."""
     q, kt, v = _f32(q), _f32(kt), _f32(v)
     rows, keys = q.shape[0], kt.shape[-1]
+    if q.shape != (rows, HD) or kt.shape != (rows, HD, keys) or v.shape != (rows, keys, HD):
+        raise ValueError(f"xattn_rows shapes q {q.shape} kt {kt.shape} v {v.shape}")
     out = np.empty((rows, HD), np.float32)
     lib().ora_xattn_rows(_p(q), _p(kt), _p(v), _p(out), rows, keys, threads)
     return out
@@ -188,6 +196,8 @@ def xattn_rows_f16(q, kt_bits, v_bits, threads=1) -> np.ndarray:
     kt_bits = np.ascontiguousarray(kt_bits, np.uint16)
     v_bits = np.ascontiguousarray(v_bits, np.uint16)
     rows, keys = q.shape[0], kt_bits.shape[-1]
+    if q.shape != (rows, HD) or kt_bits.shape != (rows, HD, keys) or v_bits.shape != (rows, keys, HD):
+        raise ValueError(f"xattn_rows_f16 shapes q {q.shape} kt {kt_bits.shape} v {v_bits.shape}")
     out = np.empty((rows, HD), np.float32)
     lib().ora_xattn_rows_f16(_p(q), _p(kt_bits, _u16p), _p(v_bits, _u16p), _p(out), rows, keys,
                              threads)
