@@ -79,6 +79,7 @@ SIGNATURES = {
     "ffai_attn_destroy": ([_vp], None),
     "ffai_attn_prefill": ([_vp, _DescP, _vp, _vp, _vp, _vp, _vp, _vp], ctypes.c_int),
     "ffai_attn_decode": ([_vp, _DescP, _vp, _vp, _vp, _vp, _vp, _i32, _vp], ctypes.c_int),
+    "ffai_attn_decode_static": ([_DescP, _vp, _vp, _vp, _vp, _vp, _i32, _vp], ctypes.c_int),
     "ffai_attn_varlen": ([_vp, _DescP, _i32p, _i32p, _i32, _vp, _vp, _vp, _vp, _vp, _vp],
                          ctypes.c_int),
     "ffai_attn_prefill_host": ([_vp, _DescP, _vp, _vp, _vp, _vp, _vp], ctypes.c_int),

@@ -150,6 +150,30 @@ def decode(q, k, v, *, scale: float = 1.0, k_layout="heads", kv_len=None, out_dt
     return (out, lse) if with_lse else out
 
 
+def decode_static(q, k, v, *, scale: float = 1.0, k_layout="heads", kv_len=None,
+                  out_dtype=torch.float32, with_lse=False, num_splits=0, causal=False,
+                  q_offset=0, out=None):
+    """decode() through ffai_attn_decode_static: no context, no allocation by
+    the library (its split scratch is a static device array), on q's device.
+    Serialise calls on one device; see the header for the limits."""
+    dev = _need_cuda(q, k, v)
+    B, H, qlen = _dims(q, "heads")
+    _, _, cap = _dims(k, k_layout)
+    Nk = cap if kv_len is None else kv_len
+    if out is None:
+        out = torch.empty((B, H, 1, 64), dtype=out_dtype, device=dev)
+    lse = torch.empty((B, H), dtype=torch.float32, device=dev) if with_lse else None
+    d = _abi.new_desc(batch=B, heads=H, q_len=qlen, kv_len=Nk, kv_capacity=cap,
+                      q_dtype=_DT[q.dtype], kv_dtype=_DT[k.dtype], out_dtype=_DT[out.dtype],
+                      k_layout=_LAYOUT[k_layout], causal=int(causal), q_offset=q_offset,
+                      scale=scale)
+    with torch.cuda.device(dev):
+        st = _abi.load().ffai_attn_decode_static(ctypes.byref(d), _ptr(q), _ptr(k), _ptr(v),
+                                                 _ptr(out), _ptr(lse), num_splits, _stream(dev))
+    _check(st, None)
+    return (out, lse) if with_lse else out
+
+
 def varlen(q, k, v, cu_seqlens_q, cu_seqlens_k=None, *, scale: float = 1.0,
            out_dtype=torch.float32, with_lse=False, out=None):
     """Ragged prefill over packed segments: q/k/v (T,H,64), host cu_seqlens.

@@ -872,3 +872,108 @@ int ffai_flash_attend_merged(ffai_attn_ctx* ctx, const ffai_tensor4* q, const ff
 }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------------------
+// Decode without a context and without allocating: the split kernel's
+// tickets and partials live in this statically allocated device array.
+//
+//   words [0, kStaticRows)                      per-row tickets; must be zero
+//                                               before a launch: zero when the
+//                                               module loads, and the last CTA
+//                                               of each row re-zeroes its
+//                                               ticket, so they stay zero
+//                                               between launches
+//   words [kStaticRows, + kStaticPartFloats)    (row, split) partials (m, l,
+//                                               o[64]); no initial value needed
+//
+// One copy per device: two launches in flight at once on one device (two
+// streams, two host threads) share it and race.
+namespace {
+constexpr int kStaticRows = 4096;                         // max batch x heads
+constexpr int kStaticSlots = 4096;                        // max rows x splits
+constexpr int kStaticPartFloats = kStaticSlots * kPartStride;
+constexpr int kStaticWords = kStaticRows + kStaticPartFloats;  // 1.07 MiB
+constexpr int kStaticMaxDevices = 64;
+}  // namespace
+
+static __device__ __align__(256) uint32_t g_decode_scratch[kStaticWords];
+
+extern "C" int ffai_attn_decode_static(const ffai_attn_desc* d, const void* q, const void* k,
+                                       const void* v, void* o, float* lse, int32_t num_splits,
+                                       void* stream) {
+  const int st = check_desc(nullptr, d, FFAI_OP_DECODE);
+  if (st) return st;
+  if (!q || !k || !v || !o) return set_error(nullptr, FFAI_ATTN_ERR_INVALID, "null operand");
+  if (num_splits < 0)
+    return set_error(nullptr, FFAI_ATTN_ERR_INVALID, "num_splits %d < 0", num_splits);
+  for (const void* ptr : {q, k, v, static_cast<const void*>(o)})
+    if (reinterpret_cast<uintptr_t>(ptr) % 16 != 0)
+      return set_error(nullptr, FFAI_ATTN_ERR_INVALID, "decode operands must be 16-byte aligned");
+  const long long rows = static_cast<long long>(d->batch) * d->heads;
+  if (rows > 65535)
+    return set_error(nullptr, FFAI_ATTN_ERR_INVALID, "decode_static: %lld rows > 65535", rows);
+  const int cap = d->kv_capacity > 0 ? d->kv_capacity : d->kv_len;
+  int kv = d->kv_len;
+  if (d->causal) kv = std::min(kv, d->q_offset + 1);
+  if (kv <= 0) return set_error(nullptr, FFAI_ATTN_ERR_INVALID, "no visible keys");
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_fail(nullptr, e, "cudaGetDevice");
+  if (dev < 0 || dev >= kStaticMaxDevices)
+    return set_error(nullptr, FFAI_ATTN_ERR_INVALID, "device %d out of range", dev);
+  // Same chunking as ffai_attn_decode's split kernel.
+  int chunk;
+  if (num_splits > 0) {
+    chunk = (kv + num_splits - 1) / num_splits;
+    chunk = std::min(std::max(chunk, 1), 128);
+  } else {
+    int sms = 0;
+    e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    if (e != cudaSuccess) return cuda_fail(nullptr, e, "cudaDeviceGetAttribute");
+    chunk = d->kv_dtype == FFAI_DT_F32 ? 64 : 128;
+    const int splits128 = (kv + chunk - 1) / chunk;
+    if (chunk == 128 && rows * splits128 < 2LL * sms && kv > 64) chunk = 64;
+  }
+  const int splits = (kv + chunk - 1) / chunk;
+  if (splits > 1 && (rows > kStaticRows || rows * splits > kStaticSlots))
+    return set_error(nullptr, FFAI_ATTN_ERR_INVALID,
+                     "decode_static: %lld rows x %d splits exceeds the static scratch "
+                     "(at most %d rows and %d rows x splits)",
+                     rows, splits, kStaticRows, kStaticSlots);
+  // Device address of the scratch, fetched once per device with it current.
+  static std::mutex mu;
+  static void* addr[kStaticMaxDevices] = {};
+  void* base = nullptr;
+  {
+    std::lock_guard<std::mutex> lock(mu);
+    if (!addr[dev]) {
+      e = cudaGetSymbolAddress(&addr[dev], g_decode_scratch);
+      if (e != cudaSuccess) {
+        addr[dev] = nullptr;
+        return cuda_fail(nullptr, e, "cudaGetSymbolAddress(g_decode_scratch)");
+      }
+    }
+    base = addr[dev];
+  }
+  DecodeParams p{};
+  p.q = q;
+  p.k = k;
+  p.v = v;
+  p.out = o;
+  p.lse = lse;
+  p.rows = static_cast<int>(rows);
+  p.kv_len = kv;
+  p.cap = cap;
+  p.chunk = chunk;
+  p.splits = splits;
+  p.q_dtype = d->q_dtype;
+  p.kv_dtype = d->kv_dtype;
+  p.out_dtype = d->out_dtype;
+  p.k_kt = d->k_layout == FFAI_LAYOUT_KT;
+  p.scale_log2 = d->scale * 1.4426950408889634f;
+  p.counters = static_cast<unsigned*>(base);
+  p.part = reinterpret_cast<float*>(static_cast<uint32_t*>(base) + kStaticRows);
+  e = launch_decode(p, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(nullptr, e, "launch_decode");
+  return FFAI_ATTN_OK;
+}

@@ -139,6 +139,28 @@ int ffai_attn_prefill(ffai_attn_ctx* ctx, const ffai_attn_desc* d, const void* q
 int ffai_attn_decode(ffai_attn_ctx* ctx, const ffai_attn_desc* d, const void* q, const void* k,
                      const void* v, void* o, float* lse, int32_t num_splits, void* stream);
 
+/* Decode as ffai_attn_decode's split kernel does (same chunking for the same
+ * num_splits, same results), but with no context and no memory allocation:
+ * it calls no cudaMalloc / cudaFree or allocating library function.  For
+ * callers that cannot allocate device memory during a decode step: a runtime
+ * whose device memory is all owned by its own caching pool, or a
+ * latency-bound streaming thread that must not block in the driver
+ * (cudaFree synchronises the device).  No reference counterpart.
+ *
+ * Runs on the calling thread's current CUDA device, which must own the
+ * buffers and `stream`.  The split partials and per-row tickets live in a
+ * static device array of the library (1.07 MiB per device): at most 4096
+ * rows (batch x heads) and 4096 rows x splits when a row is split; larger
+ * shapes return FFAI_ATTN_ERR_INVALID.  The tickets start at zero when the
+ * library's module loads and every launch leaves them at zero.  The scratch
+ * address is looked up once per device on the first call with that device
+ * current; make that first call before any stream capture.  Calls that can
+ * be in flight at the same time on one device (different streams or host
+ * threads) share the scratch and race: serialise them.  Errors and declines
+ * are reported through ffai_attn_last_error(NULL, ...). */
+int ffai_attn_decode_static(const ffai_attn_desc* d, const void* q, const void* k, const void* v,
+                            void* o, float* lse, int32_t num_splits, void* stream);
+
 /* Variable-length (ragged) prefill over packed segments, TOKEN_MAJOR
  * (T, H, 64) operands and output.  Segment s owns query rows
  * [cu_seqlens_q[s], cu_seqlens_q[s+1]) and keys [cu_seqlens_k[s],
