@@ -206,9 +206,8 @@ int check_desc(const ffai_attn_ctx* ctx, const ffai_attn_desc* d, int op) {
   const bool checked = (d->flags & FFAI_ATTN_FLAG_CHECKED_F32) != 0;
   if (checked && d->q_dtype != FFAI_DT_F32)
     return set_error(ctx, FFAI_ATTN_DECLINED, "checked-f32 mode needs f32 operands");
-  if (d->causal && !checked)
-    return set_error(ctx, FFAI_ATTN_DECLINED,
-                     "causal prefill is served by the checked-f32 kernel only");
+  if (d->causal && d->q_offset < 0)
+    return set_error(ctx, FFAI_ATTN_ERR_INVALID, "causal q_offset %d < 0", d->q_offset);
   return FFAI_ATTN_OK;
 }
 
@@ -281,12 +280,14 @@ int make_map(ffai_attn_ctx* ctx, CUtensorMap* map, const void* base, bool token_
 // units of up to 256 query rows, longest sequences first.
 int prepare_work(ffai_attn_ctx* ctx, const std::vector<int>& q_start, const std::vector<int>& q_len,
                  const std::vector<int>& k_start, const std::vector<int>& k_len, int H,
-                 cudaStream_t s) {
+                 cudaStream_t s, int causal = 0, int q_offset = 0) {
   const int nseq = static_cast<int>(q_len.size());
   std::vector<long long> key;
-  key.reserve(4 * nseq + 2);
+  key.reserve(4 * nseq + 4);
   key.push_back(H);
   key.push_back(nseq);
+  key.push_back(causal);
+  key.push_back(causal ? q_offset : 0);
   for (int i = 0; i < nseq; ++i) {
     key.push_back(q_start[i]);
     key.push_back(q_len[i]);
@@ -310,6 +311,15 @@ int prepare_work(ffai_attn_ctx* ctx, const std::vector<int>& q_start, const std:
         units.push_back(make_int4(si, h, r0, left > kTcRows ? 2 : 1));
       }
     }
+  }
+  if (causal) {
+    // Causal units differ in cost (key blocks of their tiles): longest first.
+    auto cost = [&](const int4& u) {
+      return tc_tile_blocks(1, q_offset, q_len[u.x], k_len[u.x], u.z, u.w, 0) +
+             tc_tile_blocks(1, q_offset, q_len[u.x], k_len[u.x], u.z, u.w, 1);
+    };
+    std::stable_sort(units.begin(), units.end(),
+                     [&](const int4& a, const int4& b) { return cost(a) > cost(b); });
   }
   int st = ensure(ctx, &ctx->d_units, &ctx->units_cap, units.size());
   if (st) return st;
@@ -344,7 +354,7 @@ struct Operand {
 
 int run_tc(ffai_attn_ctx* ctx, const Operand& q, const Operand& k, const Operand& v, int H,
            int ab_f16, void* o, int out_bf16, bool out_tm, long long out_rows, float* lse,
-           long long lse_tokens, float scale, cudaStream_t s) {
+           long long lse_tokens, float scale, cudaStream_t s, int causal = 0, int q_offset = 0) {
   CUtensorMap tq, tk, tv;
   int st = make_map(ctx, &tq, q.ptr, q.token_major, H, q.rows, q.groups);
   if (st) return st;
@@ -371,6 +381,8 @@ int run_tc(ffai_attn_ctx* ctx, const Operand& q, const Operand& k, const Operand
   p.lse_tokens = lse_tokens;
   p.scale_log2 = scale * 1.4426950408889634f;
   p.err = ctx->d_err;
+  p.causal = causal;
+  p.q_offset = q_offset;
   const int grid = std::min(ctx->wl_units, ctx->num_sms);
   if (grid <= 0) return FFAI_ATTN_OK;
   FFAI_CUDA(ctx, launch_prefill_tc(tq, tk, tv, p, grid, ab_f16, s));
@@ -464,7 +476,7 @@ int prefill_impl(ffai_attn_ctx* ctx, const ffai_attn_desc* d, const void* q, con
     qs[b] = b * Nq;
     ks[b] = b * cap;  // token-major K/V are never staged, so they keep `cap`
   }
-  int st = prepare_work(ctx, qs, ql, ks, kl, H, s);
+  int st = prepare_work(ctx, qs, ql, ks, kl, H, s, d->causal, d->q_offset);
   if (st) return st;
   const long long BH = static_cast<long long>(B) * H;
   Operand oq{qq, q_tm, q_tm ? static_cast<long long>(B) * Nq : Nq, BH};
@@ -472,7 +484,7 @@ int prefill_impl(ffai_attn_ctx* ctx, const ffai_attn_desc* d, const void* q, con
   Operand ov{vv, v_tm, v_tm ? static_cast<long long>(B) * vcap : vcap, BH};
   return run_tc(ctx, oq, ok, ov, H, ab_f16, o, d->out_dtype == FFAI_DT_BF16,
                 d->out_layout == FFAI_LAYOUT_TOKEN_MAJOR, Nq, lse, static_cast<long long>(B) * Nq,
-                d->scale, s);
+                d->scale, s, d->causal, d->q_offset);
 }
 
 int decode_impl(ffai_attn_ctx* ctx, const ffai_attn_desc* d, const void* q, const void* k,

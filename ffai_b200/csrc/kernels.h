@@ -96,7 +96,23 @@ struct TcParams {
   long long lse_tokens;  // token-major lse is (H, lse_tokens)
   float scale_log2;
   unsigned* err;
+  int causal;    // key j visible to query row i (within its sequence) iff j <= q_offset + i
+  int q_offset;  // >= 0
 };
+
+// Key blocks (of kTcKeys) that tile t (0, 1) of a unit needs: all of the
+// sequence's blocks, or with `causal` those up to the last row's horizon;
+// 0 for an absent tile.  Shared by the kernel and the host's work ordering.
+__host__ __device__ inline int tc_tile_blocks(int causal, int q_offset, int q_len, int k_len,
+                                              int row0, int ntiles, int t) {
+  if (t >= ntiles) return 0;
+  const int nblk = (k_len + kTcKeys - 1) / kTcKeys;
+  if (!causal) return nblk;
+  const int last = row0 + t * kTcRows + kTcRows - 1 < q_len - 1 ? row0 + t * kTcRows + kTcRows - 1
+                                                                : q_len - 1;
+  const int horizon = (q_offset + last + 1 + kTcKeys - 1) / kTcKeys;  // blocks holding keys <= q_offset+last
+  return horizon < nblk ? horizon : nblk;
+}
 
 // tm*: 3-d tensor maps built by the host for 128-row x 64-col boxes with
 // 128-byte swizzle.  ab_f16: 1 for f16 operands, 0 for bf16.

@@ -74,8 +74,15 @@ __device__ __forceinline__ void unit_at(const TcParams& p, int u, TcUnit& out) {
   out.ntiles = w.w;
 }
 
-__device__ __forceinline__ int num_blocks(const TcParams& p, int seq) {
-  return (__ldg(p.k_len + seq) + kTcKeys - 1) / kTcKeys;
+// Key blocks tile t of unit w attends (0 when the tile is absent).
+__device__ __forceinline__ int tile_blocks(const TcParams& p, const TcUnit& w, int t) {
+  return tc_tile_blocks(p.causal, p.q_offset, __ldg(p.q_len + w.seq), __ldg(p.k_len + w.seq),
+                        w.row0, w.ntiles, t);
+}
+
+// Key blocks the unit loads: those of its last tile, which sees the most.
+__device__ __forceinline__ int unit_blocks(const TcParams& p, const TcUnit& w) {
+  return tile_blocks(p, w, w.ntiles - 1);
 }
 
 // TMA coordinates of a 128-row box of (seq, head) starting at `row`.
@@ -141,7 +148,7 @@ __device__ __forceinline__ void run_producer(const CUtensorMap* tmQ, const CUten
       tma_load_3d(sQ + t * kTileBytes, tmQ, &bars->q_full[t], 0, c1, c2);
       ++q_use[t];
     }
-    const int nblk = num_blocks(p, w.seq);
+    const int nblk = unit_blocks(p, w);
     for (int j = 0; ok && j < nblk; ++j) {
       const uint32_t s = kv_cnt % kTcStages;
       if (kv_cnt >= static_cast<uint32_t>(kTcStages) &&
@@ -218,10 +225,11 @@ __device__ __forceinline__ void run_mma(const TcParams& p, int t, uint8_t* sQ, u
   if (u >= p.num_units) return;
   TcUnit cur;
   unit_at(p, u, cur);
-  int cur_nblk = num_blocks(p, cur.seq);
+  int cur_nblk = unit_blocks(p, cur);
+  int cur_tb = tile_blocks(p, cur, t);  // blocks this tile computes (a prefix of the unit's)
   int j = 0;
   uint32_t g = 0;
-  if (t < cur.ntiles && !issue_s<AB_F16>(t, true, cur_nblk == 1, g, st, sQ, sK, tmem, bars, p.err))
+  if (cur_tb > 0 && !issue_s<AB_F16>(t, true, cur_tb == 1, g, st, sQ, sK, tmem, bars, p.err))
     return;
 
   // P.V: M=128, N=64, A = P from TMEM, B = V MN-major (head dim contiguous).
@@ -229,27 +237,28 @@ __device__ __forceinline__ void run_mma(const TcParams& p, int t, uint8_t* sQ, u
   while (true) {
     // Next block in this CTA's flat sequence of (unit, key block).
     TcUnit nxt = cur;
-    int nxt_j = j + 1, nxt_nblk = cur_nblk;
+    int nxt_j = j + 1, nxt_nblk = cur_nblk, nxt_tb = cur_tb;
     bool has_next = true;
     if (nxt_j >= cur_nblk) {
       const int nu = u + gridDim.x;
       if (nu < p.num_units) {
         unit_at(p, nu, nxt);
         nxt_j = 0;
-        nxt_nblk = num_blocks(p, nxt.seq);
+        nxt_nblk = unit_blocks(p, nxt);
+        nxt_tb = tile_blocks(p, nxt, t);
       } else {
         has_next = false;
       }
     }
     // Scores of the next block first: they need only the softmax to have
     // read the current ones, and run while it exponentiates them.
-    if (has_next && t < nxt.ntiles &&
-        !issue_s<AB_F16>(t, nxt_j == 0, nxt_j == nxt_nblk - 1, g + 1, st, sQ, sK, tmem, bars,
+    if (has_next && nxt_j < nxt_tb &&
+        !issue_s<AB_F16>(t, nxt_j == 0, nxt_j == nxt_tb - 1, g + 1, st, sQ, sK, tmem, bars,
                          p.err))
       return;
     const uint32_t s = g % kTcStages;
     if (!mbar_wait(&bars->v_full[s], (g / kTcStages) & 1, abort_flag, p.err, kErrTimeoutMma)) return;
-    if (t < cur.ntiles) {
+    if (j < cur_tb) {
       if (!mbar_wait(&bars->p_full[t], st.pv_cnt[t] & 1, abort_flag, p.err, kErrTimeoutMma))
         return;
       tc_fence_after();
@@ -269,6 +278,7 @@ __device__ __forceinline__ void run_mma(const TcParams& p, int t, uint8_t* sQ, u
     if (nxt_j == 0) u += gridDim.x;
     cur = nxt;
     cur_nblk = nxt_nblk;
+    cur_tb = nxt_tb;
     j = nxt_j;
     ++g;
   }
@@ -400,7 +410,7 @@ __device__ __forceinline__ void exp_pack_rows(const float* sf, float sl2, const 
 // warps with the same w % 4.  Thread (t0, t1) = (lane % 4, lane / 4) handles
 // rows lb + t1 and lb + t1 + 8, a quarter of each row's columns; the four
 // threads of a row reduce its max and sum with two shuffles.
-template <int AB_F16>
+template <int AB_F16, bool CAUSAL>
 __device__ __forceinline__ void run_softmax(const TcParams& p, uint32_t tmem, TcBars* bars) {
   volatile int* abort_flag = &bars->abort_flag;
   const int warp = threadIdx.x / 32;
@@ -420,7 +430,15 @@ __device__ __forceinline__ void run_softmax(const TcParams& p, uint32_t tmem, Tc
     unit_at(p, u, w);
     if (t >= w.ntiles) continue;
     const int kv_len = __ldg(p.k_len + w.seq);
-    const int nblk = (kv_len + kTcKeys - 1) / kTcKeys;
+    const int nblk = CAUSAL ? tile_blocks(p, w, t) : (kv_len + kTcKeys - 1) / kTcKeys;
+    // Keys visible to this thread's two rows: all kv_len, or with `causal`
+    // those up to q_offset + row.
+    int lim[2] = {kv_len, kv_len};
+    if constexpr (CAUSAL) {
+#pragma unroll
+      for (int v = 0; v < 2; ++v)
+        lim[v] = min(kv_len, p.q_offset + w.row0 + t * kTcRows + lb + t1 + 8 * v + 1);
+    }
     float m_run[2] = {-INFINITY, -INFINITY};  // per row: log2 domain, integer-valued
     float l_run[2] = {0.f, 0.f};              // per row: this thread's share of the sum
 
@@ -436,14 +454,23 @@ __device__ __forceinline__ void run_softmax(const TcParams& p, uint32_t tmem, Tc
       mbar_arrive(&bars->sc_done[t]);
       float* sf = reinterpret_cast<float*>(sr);
 
-      const int rem = kv_len - j * kTcKeys;  // valid keys in this block
-      const bool tail = rem < kTcKeys;
+      // Valid keys of this block per row (the sequence's tail, or the causal
+      // diagonal); columns past them are -inf and exponentiate to exactly 0.
+      const int rem0 = lim[0] - j * kTcKeys, rem1 = lim[1] - j * kTcKeys;
+      const bool tail = (CAUSAL ? min(rem0, rem1) : rem0) < kTcKeys;
       if (tail) {
 #pragma unroll
         for (int k = 0; k < 16; ++k)
 #pragma unroll
-          for (int x = 0; x < 2; ++x)
-            if (8 * k + 2 * t0 + x >= rem) sf[4 * k + x] = sf[4 * k + 2 + x] = -INFINITY;
+          for (int x = 0; x < 2; ++x) {
+            const int col = 8 * k + 2 * t0 + x;
+            if constexpr (CAUSAL) {
+              if (col >= rem0) sf[4 * k + x] = -INFINITY;
+              if (col >= rem1) sf[4 * k + 2 + x] = -INFINITY;
+            } else if (col >= rem0) {
+              sf[4 * k + x] = sf[4 * k + 2 + x] = -INFINITY;
+            }
+          }
       }
       float mx[2];
 #pragma unroll
@@ -534,7 +561,7 @@ __device__ __forceinline__ void run_softmax(const TcParams& p, uint32_t tmem, Tc
   }
 }
 
-template <int AB_F16>
+template <int AB_F16, bool CAUSAL>
 __global__ void __launch_bounds__(kTcThreads, 1)
     prefill_tc_kernel(const __grid_constant__ CUtensorMap tmQ,
                       const __grid_constant__ CUtensorMap tmK,
@@ -593,7 +620,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       mbar_wait(&bars->drain, 0, &none, p.err, kErrTimeoutDrain);
     }
   } else {
-    run_softmax<AB_F16>(p, tmem, bars);
+    run_softmax<AB_F16, CAUSAL>(p, tmem, bars);
   }
 
   __syncwarp();
@@ -615,22 +642,21 @@ cudaError_t launch_prefill_tc(const CUtensorMap& tmQ, const CUtensorMap& tmK,
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return e;
-  static bool configured[2][64] = {};
+  static bool configured[4][64] = {};
   if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
-  if (!configured[ab_f16][dev]) {
-    e = ab_f16 ? cudaFuncSetAttribute(prefill_tc_kernel<1>,
-                                      cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                      static_cast<int>(kSmemBytes))
-               : cudaFuncSetAttribute(prefill_tc_kernel<0>,
-                                      cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                      static_cast<int>(kSmemBytes));
+  const int which = ab_f16 * 2 + (p.causal ? 1 : 0);
+  void (*kern)(const CUtensorMap, const CUtensorMap, const CUtensorMap, const TcParams) =
+      which == 0   ? prefill_tc_kernel<0, false>
+      : which == 1 ? prefill_tc_kernel<0, true>
+      : which == 2 ? prefill_tc_kernel<1, false>
+                   : prefill_tc_kernel<1, true>;
+  if (!configured[which][dev]) {
+    e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             static_cast<int>(kSmemBytes));
     if (e != cudaSuccess) return e;
-    configured[ab_f16][dev] = true;
+    configured[which][dev] = true;
   }
-  if (ab_f16)
-    prefill_tc_kernel<1><<<grid, kTcThreads, kSmemBytes, s>>>(tmQ, tmK, tmV, p);
-  else
-    prefill_tc_kernel<0><<<grid, kTcThreads, kSmemBytes, s>>>(tmQ, tmK, tmV, p);
+  kern<<<grid, kTcThreads, kSmemBytes, s>>>(tmQ, tmK, tmV, p);
   return cudaGetLastError();
 }
 

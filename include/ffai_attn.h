@@ -124,9 +124,13 @@ void ffai_attn_destroy(ffai_attn_ctx* ctx);
  * (flash_attn.rs:170-209, :400-405) and flash_head_strided (:429-487).
  * bf16/f16 operands run the tcgen05 tensor-core kernel; f32 operands are
  * converted to bf16 on the device first, unless FFAI_ATTN_FLAG_CHECKED_F32
- * selects the f32 SIMT kernel.  `lse` (optional, f32) receives the natural
- * log-sum-exp of each row's scaled logits: (B,H,N) for heads-split output,
- * (H, B*N) for token-major output. */
+ * selects the f32 SIMT kernel.  `causal` (q_offset >= 0) masks key j from
+ * query row i unless j <= q_offset + i: the decoder's prompt prefill over its
+ * KV cache (the reference builds this mask in causal_mask,
+ * text_decoder.rs:904-923, and declines the fused kernel for it,
+ * flash_attn.rs:219); both kernels serve it.  `lse` (optional, f32) receives
+ * the natural log-sum-exp of each row's scaled logits: (B,H,N) for
+ * heads-split output, (H, B*N) for token-major output. */
 int ffai_attn_prefill(ffai_attn_ctx* ctx, const ffai_attn_desc* d, const void* q, const void* k,
                       const void* v, void* o, float* lse, void* stream);
 

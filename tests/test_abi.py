@@ -76,8 +76,9 @@ def test_check_gate(lib):
     assert _check(lib, **{**enc, "scale": 0.0}) == _abi.ERR_INVALID
     assert _check(lib, **{**enc, "kv_capacity": 100}) == _abi.ERR_INVALID
     assert _check(lib, **{**enc, "q_layout": _abi.LAYOUT_KT}) == _abi.ERR_INVALID
-    # causal prefill: checked f32 kernel only (for now)
-    assert _check(lib, **{**enc, "causal": 1}) == _abi.DECLINED
+    # causal prefill: tensor-core and checked f32 kernels; q_offset >= 0
+    assert _check(lib, **{**enc, "causal": 1}) == _abi.OK
+    assert _check(lib, **{**enc, "causal": 1, "q_offset": -1}) == _abi.ERR_INVALID
     f32 = dict(enc, q_dtype=_abi.DT_F32, kv_dtype=_abi.DT_F32)
     assert _check(lib, **{**f32, "causal": 1, "flags": _abi.FLAG_CHECKED_F32}) == _abi.OK
     assert _check(lib, **{**enc, "flags": _abi.FLAG_CHECKED_F32}) == _abi.DECLINED

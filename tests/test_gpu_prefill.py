@@ -85,6 +85,37 @@ def test_checked_causal_vs_f64(oracle):
     assert_f32_close(f32np(out), ref, "causal")
 
 
+@pytest.mark.parametrize("B,H,Nq,q_offset,cap", [
+    (5, 12, 1, 0, 448), (5, 12, 7, 3, 448), (5, 12, 128, 0, 448), (5, 12, 129, 200, 448),
+    (2, 12, 300, 100, 448), (1, 12, 448, 0, 448), (1, 4, 1500, 0, 1500), (1, 3, 257, 1200, 1500)])
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+def test_tc_causal_vs_f64(oracle, B, H, Nq, q_offset, cap, dtype):
+    """Causal prefill on the tensor-core kernel: decoder prompts over a cache
+    of capacity `cap` (keys 0 .. q_offset + Nq - 1 live) and encoder-length
+    causal rows; row i sees keys <= q_offset + i."""
+    kv = q_offset + Nq
+    q, k, v = _inputs(B, H, Nq, dtype=dtype, seed=40 + Nq, M=cap)
+    out, lse = attention.prefill(q.to(DEV), k.to(DEV), v.to(DEV), scale=S, causal=True,
+                                 q_offset=q_offset, kv_len=kv, with_lse=True)
+    ref, ref_lse = oracle.naive_attention_f64(f32np(q), f32np(k)[:, :, :kv], f32np(v)[:, :, :kv],
+                                              scale=S, causal=True, q_offset=q_offset)
+    assert_bf16_close(f32np(out), ref, f"causal Nq={Nq} off={q_offset}")
+    # The kernel's LSE normalises the rounded 16-bit P it applies.  A row with
+    # one visible key has one P, rounded by up to 2^-8 (bf16), so its LSE may
+    # differ from the exact one by ln(1 + 2^-8) < 4e-3; long rows average out.
+    assert np.abs(f32np(lse) - ref_lse).max() <= 4e-3
+
+
+def test_tc_causal_rowsums():
+    """Applied weights of every causal row sum to 1 within 1e-6 (V = ones)."""
+    q, k, _ = _inputs(2, 4, 300, seed=44, M=448)
+    ones = torch.ones(2, 4, 448, 64, dtype=torch.bfloat16)
+    out = attention.prefill(q.to(DEV), k.to(DEV), ones.to(DEV), scale=S, causal=True,
+                            q_offset=148, kv_len=448)
+    err = (out.double() - 1.0).abs().max().item()
+    assert err <= ROWSUM_TOL, f"row sums off by {err:.2e}"
+
+
 @pytest.mark.parametrize("layout", ["token_in", "token_out", "kt", "all_token"])
 def test_tc_layouts(oracle, layout):
     q, k, v = _inputs(2, 4, 300, seed=21)
