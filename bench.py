@@ -280,6 +280,59 @@ def bench_decode(steps: int):
     return res
 
 
+def bench_ragged(dist, steps: int, peaks):
+    """c5: 256 packed segments of U{200..1500} frames, 16 heads, through the
+    varlen entry; segments assigned to ranks longest-processing-time first on
+    L^2.  Device time max over ranks; plus an end-to-end figure through the
+    public API with pinned host buffers (H2D of the packed q/k/v, D2H of the
+    output inside the timed region)."""
+    import torch
+
+    from ffai_b200 import attention, partition, workloads
+    dev = torch.device("cuda", dist.local)
+    lengths = workloads.ragged_lengths()
+    assign, load, tokens = partition.ragged_assignment(lengths, dist.world)
+    mine = assign[dist.rank]
+    q, k, v, cu = workloads.ragged_segment_inputs(lengths, mine, device=dev)
+    out = torch.empty_like(q)
+    flops_job = workloads.ragged_flops(lengths)
+    flops_rank = workloads.ragged_flops([lengths[s] for s in mine])
+
+    def step(i):
+        attention.varlen(q, k, v, cu, scale=workloads.SCALE, out=out)
+
+    for i in range(3):
+        step(i)
+    torch.cuda.synchronize()
+    t_max, t_local = timed(dist, steps, step)
+    hq, hk, hv = (t.cpu().pin_memory() for t in (q, k, v))
+    hout = torch.empty(out.shape, dtype=out.dtype, pin_memory=True)
+
+    def e2e_step(i):
+        dq, dk, dv = (t.to(dev, non_blocking=True) for t in (hq, hk, hv))
+        o = attention.varlen(dq, dk, dv, cu, scale=workloads.SCALE, out_dtype=torch.bfloat16)
+        hout.copy_(o, non_blocking=True)
+
+    e2e_step(0)
+    e_steps = max(1, min(steps, 5))
+    e_max, _ = timed(dist, e_steps, e2e_step)
+    ok = bool(torch.equal(hout, out.cpu()))
+    oks = dist.gather_objects(ok)
+    achieved = flops_rank / (t_local / steps) / 1e12
+    return {"workload": "whisper-medium-ragged-c5", "segments": len(lengths), "heads": 16,
+            "total_tokens": int(sum(lengths)), "exact_flops": flops_job,
+            "tflops": round(flops_job * steps / t_max / 1e12, 2),
+            "ms_per_step": round(t_max / steps * 1e3, 4),
+            "frac_of_peak_rank0": round(achieved / peaks["bf16_tflops"], 4),
+            "assignment": "LPT on L^2 per rank",
+            "rank_load_imbalance": round(max(load) / (sum(load) / len(load)), 4),
+            "rank_tokens": tokens,
+            "e2e_tflops": round(flops_job * e_steps / e_max / 1e12, 3),
+            "e2e_h2d_bytes_per_step": int(3 * sum(lengths) * 16 * 64 * 2),
+            "e2e_d2h_bytes_per_step": int(sum(lengths) * 16 * 64 * 2),
+            "e2e_matches_device": all(oks)}
+
+
 # ----------------------------------------------------------------- our arm
 def run_ours(args, dist):
     import numpy as np
@@ -397,6 +450,10 @@ def run_ours(args, dist):
             del raw, host_out
             shared.close(unlink=dist.rank == 0)
 
+    ragged = None
+    if not args.no_ragged:
+        ragged = bench_ragged(dist, max(5, min(args.steps, 20)), peaks)
+
     decode = None
     if dist.rank == 0 and not args.no_decode:
         decode = bench_decode(max(5, min(args.steps, 50)))
@@ -405,9 +462,19 @@ def run_ours(args, dist):
 
     cpu = None
     if dist.rank == 0 and dist.world == 1 and not args.no_cpu_baseline:
-        rate, threads, sample, _, _ = cpu_encoder_rate(cfg, budget_s=args.cpu_seconds)
+        rate, threads, sample, _, data = cpu_encoder_rate(cfg, budget_s=args.cpu_seconds)
+        # One thread on one head, as a per-core figure beside the all-threads one.
+        from oracle import oracle
+        qn, ktn, vn, _, _ = data
+        t0 = time.perf_counter()
+        runs1 = 0
+        while time.perf_counter() - t0 < 2.0 or runs1 == 0:
+            oracle.flash_units(qn[:1], ktn[:1], vn[:1], threads=1)
+            runs1 += 1
+        rate1 = 4.0 * cfg.seq * cfg.seq * 64 * runs1 / (time.perf_counter() - t0) / 1e12
         cpu = {"value": round(rate, 4), "unit": "TFLOP/s", "cores": threads, "kind": "port",
-               "sample": sample}
+               "sample": sample, "value_1_thread": round(rate1, 5),
+               "sample_1_thread": f"1 head x {cfg.seq}^2, {runs1} run(s), 1 thread"}
 
     if dist.rank == 0:
         line = {
@@ -429,6 +496,7 @@ def run_ours(args, dist):
             "gpu_launches": int(n_launch),
             "clocks": clocks.summary(),
             "decode": decode,
+            "ragged_c5": ragged,
         }
         print(json.dumps(line), flush=True)
     dist.barrier()
@@ -443,6 +511,7 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-decode", action="store_true")
+    ap.add_argument("--no-ragged", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--segments", type=int, default=0,

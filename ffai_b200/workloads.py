@@ -101,5 +101,23 @@ def ragged_inputs(lengths, heads: int = C5_HEADS, seed: int = 0, device="cpu",
     return q.to(dtype), k.to(dtype), v.to(dtype), cu
 
 
+def ragged_segment_inputs(lengths, segments, heads: int = C5_HEADS, seed: int = 0, device="cpu",
+                          dtype=torch.bfloat16):
+    """Packed q, k, v (T,H,64) and cu_seqlens of the listed `segments` only.
+
+    Segment s is drawn from its own seed (seed*100003 + s), so a rank that
+    packs a subset gets the same values as any other packing of s."""
+    qs, ks, vs, cu = [], [], [], [0]
+    for s in segments:
+        L = int(lengths[s])
+        g = _gen(seed * 100003 + 7919 + s, device)
+        qs.append(torch.randn((L, heads, HD), generator=g, device=device) * 0.5)
+        ks.append(torch.randn((L, heads, HD), generator=g, device=device) * 0.5)
+        vs.append(torch.randn((L, heads, HD), generator=g, device=device))
+        cu.append(cu[-1] + L)
+    q, k, v = torch.cat(qs), torch.cat(ks), torch.cat(vs)
+    return q.to(dtype), k.to(dtype), v.to(dtype), cu
+
+
 def ragged_flops(lengths, heads: int = C5_HEADS) -> float:
     return 4.0 * heads * HD * float(sum(int(L) * int(L) for L in lengths))
