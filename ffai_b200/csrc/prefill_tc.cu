@@ -481,25 +481,30 @@ __device__ __forceinline__ void run_softmax(const TcParams& p, uint32_t tmem, Tc
           a = max3f(a, sf[4 * k + 2 * v], sf[4 * k + 2 * v + 1]);
           b = max3f(b, sf[4 * k + 4 + 2 * v], sf[4 * k + 4 + 2 * v + 1]);
         }
-        mx[v] = fmaxf(a, b);
-        mx[v] = fmaxf(mx[v], __shfl_xor_sync(0xffffffffu, mx[v], 1));
-        mx[v] = fmaxf(mx[v], __shfl_xor_sync(0xffffffffu, mx[v], 2));
+        mx[v] = fmaxf(a, b);  // this thread's quarter of the row
       }
       // Move a row's running max only when it grows by more than 8 (a factor
       // of 256): P stays <= 256, exact in f32 sums and in bf16's exponent
       // range.  It is kept integer-valued, so corrections are exact powers of
       // two and the polynomial exp2 can fold its range reduction into the
-      // scaling FMA.
+      // scaling FMA.  A row can only grow if one of its quarters does, so
+      // the quarters' maxima are combined (shuffles) only when some thread of
+      // the warp sees growth: on a unit's first block, and rarely after.
       float corr[2] = {1.f, 1.f};
       bool grow_any = false;
+      if (__any_sync(0xffffffffu,
+                     mx[0] * sl2 > m_run[0] + 8.0f || mx[1] * sl2 > m_run[1] + 8.0f)) {
 #pragma unroll
-      for (int v = 0; v < 2; ++v) {
-        const float m_blk = mx[v] * sl2;
-        if (m_blk > m_run[v] + 8.0f) {
-          const float m_new = ceilf(m_blk);
-          corr[v] = ex2_approx(m_run[v] - m_new);  // 0 when m_run is -inf
-          m_run[v] = m_new;
-          grow_any = true;
+        for (int v = 0; v < 2; ++v) {
+          mx[v] = fmaxf(mx[v], __shfl_xor_sync(0xffffffffu, mx[v], 1));
+          mx[v] = fmaxf(mx[v], __shfl_xor_sync(0xffffffffu, mx[v], 2));
+          const float m_blk = mx[v] * sl2;
+          if (m_blk > m_run[v] + 8.0f) {
+            const float m_new = ceilf(m_blk);
+            corr[v] = ex2_approx(m_run[v] - m_new);  // 0 when m_run is -inf
+            m_run[v] = m_new;
+            grow_any = true;
+          }
         }
       }
       uint32_t pk[32];
