@@ -355,6 +355,8 @@ struct Operand {
 int run_tc(ffai_attn_ctx* ctx, const Operand& q, const Operand& k, const Operand& v, int H,
            int ab_f16, void* o, int out_bf16, bool out_tm, long long out_rows, float* lse,
            long long lse_tokens, float scale, cudaStream_t s, int causal = 0, int q_offset = 0) {
+  if (reinterpret_cast<uintptr_t>(o) % 8 != 0)
+    return set_error(ctx, FFAI_ATTN_ERR_INVALID, "prefill output must be 8-byte aligned");
   CUtensorMap tq, tk, tv;
   int st = make_map(ctx, &tq, q.ptr, q.token_major, H, q.rows, q.groups);
   if (st) return st;

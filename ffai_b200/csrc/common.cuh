@@ -72,23 +72,40 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   return ok != 0;
 }
 
+// As mbar_try_wait, but the thread may be suspended (issuing nothing) for up
+// to `hint_ns` while the phase is incomplete; it resumes when the phase
+// completes or the time is up.
+__device__ __forceinline__ bool mbar_try_wait_suspend(uint64_t* bar, uint32_t parity,
+                                                      uint32_t hint_ns) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity), "r"(hint_ns)
+      : "memory");
+  return ok != 0;
+}
+
 // Wait for the phase of `bar` with the given parity to complete.  Returns
 // false (and raises the CTA abort flag and the device error bit `code`) when
 // the wait exceeds kWaitLimitNs, or when another warp of the CTA has already
-// aborted.  Callers then skip to their teardown.
+// aborted.  Callers then skip to their teardown.  Waiting threads sleep in
+// the barrier (at most kSuspendNs per try) instead of spinning, so they take
+// no issue slots from the warps doing the work.
+constexpr uint32_t kSuspendNs = 1000000;  // 1 ms
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
                                           unsigned* err, unsigned code) {
   if (mbar_try_wait(bar, parity)) return true;
   const unsigned long long t0 = globaltimer_ns();
-  for (uint32_t n = 1;; ++n) {
-    if (mbar_try_wait(bar, parity)) return true;
-    if ((n & 63u) == 0) {
-      if (*abort_flag) return false;
-      if (globaltimer_ns() - t0 > kWaitLimitNs) {
-        *abort_flag = 1;
-        if (err) atomicOr(err, code);
-        return false;
-      }
+  while (true) {
+    if (mbar_try_wait_suspend(bar, parity, kSuspendNs)) return true;
+    if (*abort_flag) return false;
+    if (globaltimer_ns() - t0 > kWaitLimitNs) {
+      *abort_flag = 1;
+      if (err) atomicOr(err, code);
+      return false;
     }
   }
 }

@@ -250,9 +250,12 @@ __device__ __forceinline__ void run_mma(const TcParams& p, int t, uint8_t* sQ, u
         has_next = false;
       }
     }
-    // Scores of the next block first: they need only the softmax to have
-    // read the current ones, and run while it exponentiates them.
-    if (has_next && nxt_j < nxt_tb &&
+    // Across a unit boundary the order flips: the unit's last P.V goes
+    // first, since the softmax waits for it before its epilogue, which
+    // leaves the next unit's first scores plenty of time.
+    const bool next_first = has_next && nxt_j < nxt_tb;
+    const bool boundary = nxt_j == 0;
+    if (next_first && !boundary &&
         !issue_s<AB_F16>(t, nxt_j == 0, nxt_j == nxt_tb - 1, g + 1, st, sQ, sK, tmem, bars,
                          p.err))
       return;
@@ -274,6 +277,9 @@ __device__ __forceinline__ void run_mma(const TcParams& p, int t, uint8_t* sQ, u
     } else {
       mbar_arrive(&bars->kv_empty[s]);
     }
+    if (next_first && boundary &&
+        !issue_s<AB_F16>(t, true, nxt_tb == 1, g + 1, st, sQ, sK, tmem, bars, p.err))
+      return;
     if (!has_next) break;
     if (nxt_j == 0) u += gridDim.x;
     cur = nxt;
