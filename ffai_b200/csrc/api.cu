@@ -321,6 +321,26 @@ int prepare_work(ffai_attn_ctx* ctx, const std::vector<int>& q_start, const std:
     std::stable_sort(units.begin(), units.end(),
                      [&](const int4& a, const int4& b) { return cost(a) > cost(b); });
   }
+  // Persistent CTAs take units u, u + G, u + 2G, ...: a last wave of r < G / 2
+  // units leaves most SMs idle while r finish.  Splitting those r two-tile
+  // units into 2r one-tile units (at the end of the list, so the full waves
+  // keep their CTAs) lets the last wave finish in about the time of one tile.
+  const long long G = std::min<long long>(static_cast<long long>(units.size()), ctx->num_sms);
+  if (G > 0 && static_cast<long long>(units.size()) > G) {
+    const long long r = static_cast<long long>(units.size()) % G;
+    if (r > 0 && 2 * r <= G) {
+      std::vector<int4> tail(units.end() - r, units.end());
+      units.resize(units.size() - r);
+      for (const int4& t : tail) {
+        if (t.w == 2) {
+          units.push_back(make_int4(t.x, t.y, t.z, 1));
+          units.push_back(make_int4(t.x, t.y, t.z + kTcRows, 1));
+        } else {
+          units.push_back(t);
+        }
+      }
+    }
+  }
   int st = ensure(ctx, &ctx->d_units, &ctx->units_cap, units.size());
   if (st) return st;
   st = ensure(ctx, &ctx->d_seq, &ctx->seq_cap, 4 * static_cast<size_t>(nseq));
