@@ -224,6 +224,67 @@ def prefill_host(q, k, v, *, device: int = 0, scale: float = 1.0, out_dtype=torc
     return out
 
 
+_worker_contexts: dict = {}
+
+
+def worker_contexts(devices) -> list:
+    """One library context per entry of `devices` (a device may repeat: each
+    repetition gets a context of its own), created once and kept."""
+    out, seen = [], {}
+    with _ctx_lock:
+        for dev in devices:
+            slot = seen.get(dev, 0)
+            seen[dev] = slot + 1
+            ctx = _worker_contexts.get((dev, slot))
+            if ctx is None:
+                st = ctypes.c_int(0)
+                ctx = _abi.load().ffai_attn_create(dev, ctypes.byref(st))
+                if not ctx:
+                    raise AttnError(st.value, _abi.last_error(None))
+                _worker_contexts[(dev, slot)] = ctx
+            out.append(ctx)
+    return out
+
+
+def multi_prefill_host(q, k, v, *, devices, scale: float = 1.0, out_dtype=torch.float32,
+                       chunk_segments: int = 0, out=None, lse=None):
+    """prefill_host over several devices: one worker thread per entry of
+    `devices` takes chunks of `chunk_segments` sequences from a shared queue;
+    a worker that fails hands its chunk back to the others.  Returns
+    (out, failed_workers)."""
+    for t in (q, k, v):
+        if t.device.type != "cpu" or not t.is_contiguous():
+            raise ValueError("multi_prefill_host takes contiguous host tensors")
+    B, H, Nq = _dims(q, "heads")
+    _, _, Nk = _dims(k, "heads")
+    if out is None:
+        out = torch.empty((B, H, Nq, 64), dtype=out_dtype, pin_memory=q.is_pinned())
+    d = _abi.new_desc(batch=B, heads=H, q_len=Nq, kv_len=Nk, q_dtype=_DT[q.dtype],
+                      kv_dtype=_DT[k.dtype], out_dtype=_DT[out.dtype], scale=scale)
+    ctxs = worker_contexts(list(devices))
+    arr = (ctypes.c_void_p * len(ctxs))(*ctxs)
+    failed = ctypes.c_int32(0)
+    st = _abi.load().ffai_attn_multi_prefill_host(arr, len(ctxs), ctypes.byref(d), _ptr(q), _ptr(k),
+                                                  _ptr(v), _ptr(out), _ptr(lse), chunk_segments,
+                                                  ctypes.byref(failed))
+    _check(st, None)
+    return out, failed.value
+
+
+def profile(device: int = 0, enable: int = -1, read: bool = True):
+    """Turn the context's launch timing on (1) / off (0) / leave it (-1);
+    with `read`, return {op: (total ms, calls)} since the last read."""
+    ctx = context(device)
+    ms = (ctypes.c_double * 3)()
+    n = (ctypes.c_int64 * 3)()
+    st = _abi.load().ffai_attn_profile(ctx, enable, ms if read else None, n if read else None)
+    _check(st, ctx)
+    if not read:
+        return None
+    names = ("prefill", "decode", "varlen")
+    return {names[i]: (ms[i], n[i]) for i in range(3)}
+
+
 def sync(device: int | None = None) -> None:
     """Synchronise the current stream and raise if an in-kernel wait timed out."""
     dev = torch.cuda.current_device() if device is None else device

@@ -6,13 +6,20 @@
 #include <cudaTypedefs.h>
 
 #include <algorithm>
+#include <chrono>
+#include <condition_variable>
 #include <cstdarg>
 #include <cstdio>
 #include <cstdlib>
 #include <cstring>
+#include <deque>
+#include <functional>
 #include <mutex>
 #include <string>
+#include <thread>
 #include <vector>
+
+#include <nvtx3/nvToolsExt.h>
 
 #include "../../include/ffai_attn.h"
 #include "kernels.h"
@@ -79,6 +86,16 @@ struct ffai_attn_ctx {
   ffai_attn_ctx* pipe_ctx = nullptr;  // inner context used for the pipeline's kernels
   std::string last_error;
   int last_status = FFAI_ATTN_OK;
+  // opt-in launch timing (FFAI_ATTN_PROFILE=1 or ffai_attn_profile): CUDA
+  // events around each prefill / decode / varlen call, and NVTX ranges
+  struct ProfRec {
+    int op;
+    cudaEvent_t a, b;
+  };
+  bool prof = false;
+  std::vector<ProfRec> prof_pending;
+  double prof_ms[3] = {0, 0, 0};
+  long long prof_n[3] = {0, 0, 0};
 };
 
 namespace {
@@ -640,6 +657,7 @@ ffai_attn_ctx* ffai_attn_create(int device, int* status) {
   std::call_once(g_encode_once, init_encoder);
   auto* ctx = new ffai_attn_ctx();
   ctx->device = device;
+  ctx->prof = env_on("FFAI_ATTN_PROFILE");
   ctx->num_sms = prop.multiProcessorCount;
   if (cudaMalloc(&ctx->d_err, sizeof(unsigned)) != cudaSuccess ||
       cudaMemset(ctx->d_err, 0, sizeof(unsigned)) != cudaSuccess) {
@@ -671,7 +689,73 @@ void ffai_attn_destroy(ffai_attn_ctx* ctx) {
   if (ctx->s_h2d) cudaStreamDestroy(ctx->s_h2d);
   if (ctx->s_comp) cudaStreamDestroy(ctx->s_comp);
   if (ctx->s_d2h) cudaStreamDestroy(ctx->s_d2h);
+  for (auto& r : ctx->prof_pending) {
+    cudaEventDestroy(r.a);
+    cudaEventDestroy(r.b);
+  }
   delete ctx;
+}
+
+}  // extern "C"
+
+namespace {
+
+// Brackets one entry-point call with CUDA events (on its stream) and an NVTX
+// range when the context's profiling is on; otherwise does nothing.
+struct ProfScope {
+  ffai_attn_ctx* ctx;
+  int op;
+  cudaStream_t s;
+  cudaEvent_t a = nullptr, b = nullptr;
+  ProfScope(ffai_attn_ctx* c, int o, cudaStream_t st, const char* name) : ctx(c), op(o), s(st) {
+    if (!ctx->prof) return;
+    nvtxRangePushA(name);
+    if (cudaEventCreate(&a) != cudaSuccess || cudaEventCreate(&b) != cudaSuccess ||
+        cudaEventRecord(a, s) != cudaSuccess) {
+      if (a) cudaEventDestroy(a);
+      if (b) cudaEventDestroy(b);
+      a = b = nullptr;
+    }
+  }
+  ~ProfScope() {
+    if (!ctx->prof) return;
+    if (a && cudaEventRecord(b, s) == cudaSuccess) {
+      ctx->prof_pending.push_back({op, a, b});
+    } else {
+      if (a) cudaEventDestroy(a);
+      if (b) cudaEventDestroy(b);
+    }
+    nvtxRangePop();
+  }
+};
+
+}  // namespace
+
+extern "C" {
+
+int ffai_attn_profile(ffai_attn_ctx* ctx, int32_t enable, double* ms, int64_t* launches) {
+  if (!ctx) return set_error(nullptr, FFAI_ATTN_ERR_INVALID, "null context");
+  DeviceGuard g(ctx->device);
+  if (ms || launches) {
+    for (auto& r : ctx->prof_pending) {
+      float t = 0.f;
+      if (cudaEventSynchronize(r.b) == cudaSuccess && cudaEventElapsedTime(&t, r.a, r.b) == cudaSuccess) {
+        ctx->prof_ms[r.op] += t;
+        ctx->prof_n[r.op] += 1;
+      }
+      cudaEventDestroy(r.a);
+      cudaEventDestroy(r.b);
+    }
+    ctx->prof_pending.clear();
+    for (int i = 0; i < 3; ++i) {
+      if (ms) ms[i] = ctx->prof_ms[i];
+      if (launches) launches[i] = ctx->prof_n[i];
+      ctx->prof_ms[i] = 0;
+      ctx->prof_n[i] = 0;
+    }
+  }
+  if (enable >= 0) ctx->prof = enable != 0;
+  return FFAI_ATTN_OK;
 }
 
 int ffai_attn_prefill(ffai_attn_ctx* ctx, const ffai_attn_desc* d, const void* q, const void* k,
@@ -681,6 +765,7 @@ int ffai_attn_prefill(ffai_attn_ctx* ctx, const ffai_attn_desc* d, const void* q
   if (st) return st;
   if (!q || !k || !v || !o) return set_error(ctx, FFAI_ATTN_ERR_INVALID, "null operand");
   DeviceGuard g(ctx->device);
+  ProfScope ps(ctx, FFAI_OP_PREFILL, static_cast<cudaStream_t>(stream), "ffai_attn_prefill");
   return prefill_impl(ctx, d, q, k, v, o, lse, static_cast<cudaStream_t>(stream));
 }
 
@@ -691,6 +776,7 @@ int ffai_attn_decode(ffai_attn_ctx* ctx, const ffai_attn_desc* d, const void* q,
   if (st) return st;
   if (!q || !k || !v || !o) return set_error(ctx, FFAI_ATTN_ERR_INVALID, "null operand");
   DeviceGuard g(ctx->device);
+  ProfScope ps(ctx, FFAI_OP_DECODE, static_cast<cudaStream_t>(stream), "ffai_attn_decode");
   return decode_impl(ctx, d, q, k, v, o, lse, num_splits, static_cast<cudaStream_t>(stream));
 }
 
@@ -716,6 +802,7 @@ int ffai_attn_varlen(ffai_attn_ctx* ctx, const ffai_attn_desc* d, const int32_t*
   const long long Tq = cu_q[n_seg], Tk = cu_k[n_seg];
   DeviceGuard g(ctx->device);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
+  ProfScope ps(ctx, FFAI_OP_VARLEN, s, "ffai_attn_varlen");
   st = prepare_work(ctx, qs, ql, ks, kl, d->heads, s);
   if (st) return st;
   if (Tq == 0) return FFAI_ATTN_OK;
@@ -805,6 +892,149 @@ int ffai_attn_prefill_host(ffai_attn_ctx* ctx, const ffai_attn_desc* d, const vo
     return set_error(ctx, FFAI_ATTN_ERR_TIMEOUT, "in-kernel wait timed out (error bits 0x%x)", err);
   }
   return FFAI_ATTN_OK;
+}
+
+}  // extern "C"
+
+namespace {
+
+// Chunks [0, n_chunks) run on n_workers host threads: worker w starts with
+// chunk w, then takes chunks from one queue.  A worker whose `work` fails
+// puts the chunk back at the front,
+// records the status and retires; the surviving workers drain the queue
+// (a worker waits while the queue is empty but others are still busy, since
+// a failing one may hand its chunk back).  Returns FFAI_ATTN_OK when every
+// chunk completed, else the first failure.  owner[c] (optional) receives the
+// worker that completed chunk c; *failed (optional) the number of workers
+// that failed.
+int run_chunk_queue(int n_workers, int n_chunks, const std::function<int(int, int)>& work,
+                    int32_t* owner, int32_t* failed) {
+  std::mutex mu;
+  std::condition_variable cv;
+  std::deque<int> queue;
+  for (int c = n_workers; c < n_chunks; ++c) queue.push_back(c);
+  int done = 0, first_err = FFAI_ATTN_OK, n_failed = 0;
+  int busy = std::min(n_workers, n_chunks);  // the workers' first chunks
+  std::vector<std::thread> threads;
+  threads.reserve(n_workers);
+  for (int w = 0; w < n_workers; ++w) {
+    threads.emplace_back([&, w] {
+      int c = w < n_chunks ? w : -1;
+      while (true) {
+        if (c < 0) {
+          std::unique_lock<std::mutex> lock(mu);
+          cv.wait(lock, [&] { return !queue.empty() || busy == 0; });
+          if (queue.empty()) return;
+          c = queue.front();
+          queue.pop_front();
+          ++busy;
+        }
+        const int st = work(w, c);
+        std::lock_guard<std::mutex> lock(mu);
+        --busy;
+        if (st == FFAI_ATTN_OK) {
+          ++done;
+          if (owner) owner[c] = w;
+          c = -1;
+          cv.notify_all();
+        } else {
+          queue.push_front(c);
+          if (first_err == FFAI_ATTN_OK) first_err = st;
+          ++n_failed;
+          cv.notify_all();
+          return;
+        }
+      }
+    });
+  }
+  for (auto& t : threads) t.join();
+  if (failed) *failed = n_failed;
+  if (done == n_chunks) return FFAI_ATTN_OK;
+  return first_err != FFAI_ATTN_OK ? first_err : FFAI_ATTN_ERR_INVALID;
+}
+
+// FFAI_ATTN_FAULT_WORKER=i makes worker i of the multi-device entry fail its
+// first chunk on the host, before any copy or launch (fault injection for
+// the re-queue path; no GPU is faulted).
+int fault_worker() {
+  const char* s = std::getenv("FFAI_ATTN_FAULT_WORKER");
+  if (!s || !*s) return -1;
+  char* end = nullptr;
+  const long v = std::strtol(s, &end, 10);
+  return (end && *end == 0 && v >= 0) ? static_cast<int>(v) : -1;
+}
+
+}  // namespace
+
+extern "C" {
+
+int ffai_attn_multi_prefill_host(ffai_attn_ctx* const* ctxs, int32_t n_ctx,
+                                 const ffai_attn_desc* d, const void* q, const void* k,
+                                 const void* v, void* o, float* lse, int32_t chunk_segments,
+                                 int32_t* failed_workers) {
+  if (!ctxs || n_ctx <= 0) return set_error(nullptr, FFAI_ATTN_ERR_INVALID, "no contexts");
+  for (int i = 0; i < n_ctx; ++i)
+    if (!ctxs[i]) return set_error(nullptr, FFAI_ATTN_ERR_INVALID, "context %d is null", i);
+  int st = check_desc(nullptr, d, FFAI_OP_PREFILL);
+  if (st) return st;
+  if (!q || !k || !v || !o) return set_error(nullptr, FFAI_ATTN_ERR_INVALID, "null operand");
+  if (lse && d->out_layout == FFAI_LAYOUT_TOKEN_MAJOR)
+    return set_error(nullptr, FFAI_ATTN_DECLINED, "host prefill: lse needs heads-split output");
+  const int B = d->batch, H = d->heads, Nq = d->q_len;
+  const int cap = d->kv_capacity > 0 ? d->kv_capacity : d->kv_len;
+  const int chunk = chunk_segments > 0 ? std::min(chunk_segments, B) : (B + n_ctx - 1) / n_ctx;
+  const int n_chunks = (B + chunk - 1) / chunk;
+  // Every layout keeps one sequence contiguous: chunk c is a byte range.
+  const size_t qb = static_cast<size_t>(H) * Nq * kHD * dtype_size(d->q_dtype);
+  const size_t kb = static_cast<size_t>(H) * cap * kHD * dtype_size(d->kv_dtype);
+  const size_t ob = static_cast<size_t>(H) * Nq * kHD * dtype_size(d->out_dtype);
+  const size_t lb = static_cast<size_t>(H) * Nq;
+  const int faulty = fault_worker();
+  std::vector<char> faulted(n_ctx, 0);
+  std::vector<std::string> errors(n_ctx);
+  auto work = [&](int w, int c) -> int {
+    if (w == faulty && !faulted[w]) {
+      faulted[w] = 1;
+      errors[w] = "injected host-side fault";
+      return set_error(ctxs[w], FFAI_ATTN_ERR_CUDA, "worker %d: injected host-side fault", w);
+    }
+    const int b0 = c * chunk, nb = std::min(chunk, B - b0);
+    ffai_attn_desc dc = *d;
+    dc.batch = nb;
+    const int r = ffai_attn_prefill_host(
+        ctxs[w], &dc, static_cast<const uint8_t*>(q) + b0 * qb,
+        static_cast<const uint8_t*>(k) + b0 * kb, static_cast<const uint8_t*>(v) + b0 * kb,
+        static_cast<uint8_t*>(o) + b0 * ob, lse ? lse + b0 * lb : nullptr);
+    if (r != FFAI_ATTN_OK) errors[w] = ctxs[w]->last_error;
+    return r;
+  };
+  int32_t n_failed = 0;
+  st = run_chunk_queue(n_ctx, n_chunks, work, nullptr, &n_failed);
+  if (failed_workers) *failed_workers = n_failed;
+  if (st != FFAI_ATTN_OK) {
+    std::string all;
+    for (int i = 0; i < n_ctx; ++i)
+      if (!errors[i].empty()) all += " [worker " + std::to_string(i) + ": " + errors[i] + "]";
+    return set_error(nullptr, st, "multi-device prefill: no worker left for the remaining "
+                     "segments;%s", all.c_str());
+  }
+  return FFAI_ATTN_OK;
+}
+
+int ffai_attn_chunk_queue_selftest(int32_t n_workers, int32_t n_chunks, uint32_t fail_mask,
+                                   int32_t* owner, int32_t* failed_workers) {
+  if (n_workers <= 0 || n_workers > 32 || n_chunks < 0)
+    return set_error(nullptr, FFAI_ATTN_ERR_INVALID, "selftest: 1..32 workers");
+  std::vector<char> faulted(n_workers, 0);
+  auto work = [&](int w, int) -> int {
+    if (((fail_mask >> w) & 1u) && !faulted[w]) {
+      faulted[w] = 1;
+      return FFAI_ATTN_ERR_CUDA;
+    }
+    std::this_thread::sleep_for(std::chrono::microseconds(200));
+    return FFAI_ATTN_OK;
+  };
+  return run_chunk_queue(n_workers, n_chunks, work, owner, failed_workers);
 }
 
 int ffai_attn_sync(ffai_attn_ctx* ctx, void* stream) {

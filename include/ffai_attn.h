@@ -188,6 +188,42 @@ int ffai_attn_varlen(ffai_attn_ctx* ctx, const ffai_attn_desc* d, const int32_t*
 int ffai_attn_prefill_host(ffai_attn_ctx* ctx, const ffai_attn_desc* d, const void* q,
                            const void* k, const void* v, void* o, float* lse);
 
+/* Multi-device host-buffer prefill (the host side of segment sharding).
+ * The batch's sequences are cut into chunks of `chunk_segments` (0: one
+ * chunk per context); n_ctx worker threads, one per context (a context per
+ * GPU, or several on one GPU), take chunks from a shared queue and run each
+ * through ffai_attn_prefill_host, which writes the chunk's rows straight into
+ * the host output (the host gather; no collective, no peer traffic).  A
+ * worker whose chunk fails hands the chunk back and retires; the surviving
+ * workers finish the batch, and the call still returns FFAI_ATTN_OK.
+ * *failed_workers (optional) receives the number of workers that failed.
+ * The environment variable FFAI_ATTN_FAULT_WORKER=i makes worker i fail its
+ * first chunk on the host, before any copy or launch (fault injection).
+ * No reference counterpart: the reference runs one window at a time
+ * (text_decoder.rs:1069-1076). */
+int ffai_attn_multi_prefill_host(ffai_attn_ctx* const* ctxs, int32_t n_ctx,
+                                 const ffai_attn_desc* d, const void* q, const void* k,
+                                 const void* v, void* o, float* lse, int32_t chunk_segments,
+                                 int32_t* failed_workers);
+
+/* Self-test of ffai_attn_multi_prefill_host's chunk queue without a GPU:
+ * n_workers (1..32) threads take n_chunks chunks; worker w fails its first
+ * chunk when bit w of fail_mask is set.  owner[c] (optional) receives the
+ * worker that completed chunk c.  Returns FFAI_ATTN_OK when every chunk
+ * completed.  Test infrastructure; no reference counterpart. */
+int ffai_attn_chunk_queue_selftest(int32_t n_workers, int32_t n_chunks, uint32_t fail_mask,
+                                   int32_t* owner, int32_t* failed_workers);
+
+/* Opt-in launch timing: with profiling on (this call with enable = 1, or
+ * FFAI_ATTN_PROFILE=1 when the context is created) every prefill, decode and
+ * varlen call on `ctx` is bracketed by CUDA events on its stream and an NVTX
+ * range.  With ms / launches non-null, the call waits for the recorded
+ * events, writes the total milliseconds and call counts per operation
+ * (index FFAI_OP_PREFILL, FFAI_OP_DECODE, FFAI_OP_VARLEN) and resets them.
+ * enable: 1 on, 0 off, -1 unchanged.  The reference's counterpart is its
+ * FFAI_PROFILE stage counters (profile.rs:1-32). */
+int ffai_attn_profile(ffai_attn_ctx* ctx, int32_t enable, double* ms, int64_t* launches);
+
 /* Synchronise `stream` and report the device error word: FFAI_ATTN_OK, or
  * FFAI_ATTN_ERR_TIMEOUT if an in-kernel bounded wait gave up since the last
  * call (the word is then cleared), or FFAI_ATTN_ERR_CUDA. */

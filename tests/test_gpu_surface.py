@@ -106,3 +106,19 @@ def test_serves_matches_reference_predicate(oracle):
         kt = torch.empty(1, 6, HD, keys, device=DEV)
         v = torch.empty(1, heads_v, keys, HD, device=DEV)
         assert flash_attn.serves(kt, v) == oracle.serves(kt.shape, v.shape)
+
+
+def test_profile_counts_calls():
+    """Opt-in launch timing: CUDA events per call, read and reset."""
+    from ffai_b200 import attention, workloads
+    attention.profile(0, enable=1)  # on; also clears earlier records
+    q, k, v = workloads.decode_inputs(448, seed=30, device="cuda")
+    for _ in range(3):
+        attention.decode(q, k, v)
+    g = torch.Generator().manual_seed(1)
+    x = (torch.randn(1, 2, 256, 64, generator=g) * 0.5).to(torch.bfloat16).cuda()
+    attention.prefill(x, x, x, scale=0.125)
+    stats = attention.profile(0, enable=0)
+    assert stats["decode"][1] == 3 and stats["decode"][0] > 0
+    assert stats["prefill"][1] == 1 and stats["prefill"][0] > 0
+    assert attention.profile(0)["decode"] == (0.0, 0)
