@@ -83,6 +83,10 @@ SIGNATURES = {
     "ffai_attn_multi_prefill_host": ([ctypes.POINTER(_vp), _i32, _DescP, _vp, _vp, _vp, _vp, _vp,
                                       _i32, _i32p], ctypes.c_int),
     "ffai_attn_chunk_queue_selftest": ([_i32, _i32, ctypes.c_uint32, _i32p, _i32p], ctypes.c_int),
+    "ffai_attn_decode_paged": ([_vp, _DescP, _vp, _vp, _vp, _i32, _vp, _vp, _i32, _vp, _vp, _vp],
+                               ctypes.c_int),
+    "ffai_kv_append": ([_vp, _DescP, _vp, _vp, _i32, _vp, _vp, _i32, _vp, _vp, _vp], ctypes.c_int),
+    "ffai_kv_copy_pages": ([_vp, _DescP, _vp, _vp, _i32, _vp, _vp, _i32, _vp], ctypes.c_int),
     "ffai_attn_profile": ([_vp, _i32, ctypes.POINTER(ctypes.c_double),
                            ctypes.POINTER(ctypes.c_int64)], ctypes.c_int),
     "ffai_attn_varlen": ([_vp, _DescP, _i32p, _i32p, _i32, _vp, _vp, _vp, _vp, _vp, _vp],

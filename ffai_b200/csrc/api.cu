@@ -1045,8 +1045,107 @@ int ffai_attn_sync(ffai_attn_ctx* ctx, void* stream) {
   FFAI_CUDA(ctx, cudaMemcpy(&err, ctx->d_err, sizeof err, cudaMemcpyDeviceToHost));
   if (err) {
     FFAI_CUDA(ctx, cudaMemset(ctx->d_err, 0, sizeof(unsigned)));
+    if (err & kErrBadArgs)
+      return set_error(ctx, FFAI_ATTN_ERR_INVALID,
+                       "a paged-cache call met a page id outside the pool or a length past its "
+                       "block table (error bits 0x%x)", err);
     return set_error(ctx, FFAI_ATTN_ERR_TIMEOUT, "in-kernel wait timed out (error bits 0x%x)", err);
   }
+  return FFAI_ATTN_OK;
+}
+
+namespace {
+
+int paged_params(ffai_attn_ctx* ctx, const ffai_attn_desc* d, const void* k_pool,
+                 const void* v_pool, int32_t num_pages, const int32_t* block_table,
+                 const int32_t* seq_lens, int32_t max_pages, DecodeParams& p) {
+  if (!ctx) return set_error(nullptr, FFAI_ATTN_ERR_INVALID, "null context");
+  if (!d) return set_error(ctx, FFAI_ATTN_ERR_INVALID, "null descriptor");
+  if (d->head_dim != kHD)
+    return set_error(ctx, FFAI_ATTN_DECLINED, "head_dim %d: only 64 is served", d->head_dim);
+  if (d->batch <= 0 || d->heads <= 0)
+    return set_error(ctx, FFAI_ATTN_ERR_INVALID, "batch %d, heads %d must be >= 1", d->batch,
+                     d->heads);
+  if (!valid_dtype(d->kv_dtype)) return set_error(ctx, FFAI_ATTN_ERR_INVALID, "unknown kv dtype");
+  if (!k_pool || !v_pool || !block_table || !seq_lens || num_pages <= 0 || max_pages <= 0)
+    return set_error(ctx, FFAI_ATTN_ERR_INVALID, "paged cache: null pointer or empty pool/table");
+  for (const void* ptr : {k_pool, v_pool})
+    if (reinterpret_cast<uintptr_t>(ptr) % 16 != 0)
+      return set_error(ctx, FFAI_ATTN_ERR_INVALID, "page pools must be 16-byte aligned");
+  p = DecodeParams{};
+  p.k = k_pool;
+  p.v = v_pool;
+  p.rows = d->batch * d->heads;
+  p.q_dtype = d->q_dtype;
+  p.kv_dtype = d->kv_dtype;
+  p.out_dtype = d->out_dtype;
+  p.scale_log2 = d->scale * 1.4426950408889634f;
+  p.err = ctx->d_err;
+  p.block_table = block_table;
+  p.seq_lens = seq_lens;
+  p.max_pages = max_pages;
+  p.num_pages = num_pages;
+  p.heads = d->heads;
+  return FFAI_ATTN_OK;
+}
+
+}  // namespace
+
+int ffai_attn_decode_paged(ffai_attn_ctx* ctx, const ffai_attn_desc* d, const void* q,
+                           const void* k_pool, const void* v_pool, int32_t num_pages,
+                           const int32_t* block_table, const int32_t* seq_lens, int32_t max_pages,
+                           void* o, float* lse, void* stream) {
+  DecodeParams p;
+  int st = paged_params(ctx, d, k_pool, v_pool, num_pages, block_table, seq_lens, max_pages, p);
+  if (st) return st;
+  if (d->q_len != 1) return set_error(ctx, FFAI_ATTN_DECLINED, "decode: q_len must be 1");
+  if (d->q_dtype != FFAI_DT_F32 && d->q_dtype != d->kv_dtype)
+    return set_error(ctx, FFAI_ATTN_DECLINED, "decode: q must be f32 or the cache dtype");
+  if (d->out_dtype != FFAI_DT_F32 && d->out_dtype != FFAI_DT_BF16)
+    return set_error(ctx, FFAI_ATTN_DECLINED, "out_dtype %d: f32 or bf16 only", d->out_dtype);
+  if (!(d->scale > 0.f) || !std::isfinite(d->scale))
+    return set_error(ctx, FFAI_ATTN_ERR_INVALID, "scale must be finite and > 0");
+  if (!q || !o) return set_error(ctx, FFAI_ATTN_ERR_INVALID, "null operand");
+  for (const void* ptr : {q, static_cast<const void*>(o)})
+    if (reinterpret_cast<uintptr_t>(ptr) % 16 != 0)
+      return set_error(ctx, FFAI_ATTN_ERR_INVALID, "decode operands must be 16-byte aligned");
+  DeviceGuard g(ctx->device);
+  ProfScope ps(ctx, FFAI_OP_DECODE, static_cast<cudaStream_t>(stream), "ffai_attn_decode_paged");
+  // Keys bound for the split: d->kv_len when given, else the table's reach.
+  const long long bound = d->kv_len > 0 ? d->kv_len : static_cast<long long>(max_pages) * kPageKeys;
+  int S = static_cast<int>(std::min<long long>(kDecodeMaxCluster, 2LL * ctx->num_sms / p.rows));
+  S = std::max(1, std::min<int>(S, static_cast<int>((bound + kPageKeys - 1) / kPageKeys)));
+  p.q = q;
+  p.out = o;
+  p.lse = lse;
+  p.kv_len = static_cast<int>(std::min<long long>(bound, 1LL << 30));
+  FFAI_CUDA(ctx, launch_decode_paged(p, S, static_cast<cudaStream_t>(stream)));
+  return FFAI_ATTN_OK;
+}
+
+int ffai_kv_append(ffai_attn_ctx* ctx, const ffai_attn_desc* d, void* k_pool, void* v_pool,
+                   int32_t num_pages, const int32_t* block_table, int32_t* seq_lens,
+                   int32_t max_pages, const void* k_new, const void* v_new, void* stream) {
+  DecodeParams p;
+  int st = paged_params(ctx, d, k_pool, v_pool, num_pages, block_table, seq_lens, max_pages, p);
+  if (st) return st;
+  if (!k_new || !v_new) return set_error(ctx, FFAI_ATTN_ERR_INVALID, "null key or value");
+  DeviceGuard g(ctx->device);
+  FFAI_CUDA(ctx, launch_kv_append(p, d->batch, k_new, v_new, static_cast<cudaStream_t>(stream)));
+  return FFAI_ATTN_OK;
+}
+
+int ffai_kv_copy_pages(ffai_attn_ctx* ctx, const ffai_attn_desc* d, void* k_pool, void* v_pool,
+                       int32_t num_pages, const int32_t* src_pages, const int32_t* dst_pages,
+                       int32_t n, void* stream) {
+  DecodeParams p;
+  static const int32_t kOne = 0;
+  int st = paged_params(ctx, d, k_pool, v_pool, num_pages, &kOne, &kOne, 1, p);
+  if (st) return st;
+  if (n < 0 || (n > 0 && (!src_pages || !dst_pages)))
+    return set_error(ctx, FFAI_ATTN_ERR_INVALID, "page copy: bad page lists");
+  DeviceGuard g(ctx->device);
+  FFAI_CUDA(ctx, launch_kv_copy_pages(p, src_pages, dst_pages, n, static_cast<cudaStream_t>(stream)));
   return FFAI_ATTN_OK;
 }
 

@@ -9,17 +9,10 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include "kernels.h"  // error bits of the device error word
+
 namespace ffai {
 
-// Error bits written to the context's device error word.
-enum : unsigned {
-  kErrTimeoutProducer = 1u << 0,
-  kErrTimeoutMma = 1u << 1,
-  kErrTimeoutSoftmax = 1u << 2,
-  kErrTimeoutDrain = 1u << 3,
-  kErrTimeoutConsumer = 1u << 4,
-  kErrBadArgs = 1u << 8,
-};
 
 // Every spin-wait gives up after this long, sets an error bit and lets the
 // kernel tear down (a kernel normally waits microseconds).

@@ -311,7 +311,7 @@ __device__ __forceinline__ void load8_f32(const T* src, float (&x)[8]) {
   }
 }
 
-template <typename T>
+template <typename T, bool PAGED>
 __global__ void __launch_bounds__(kClThreads, 2) decode_cluster_kernel(DecodeParams p, int S,
                                                                         int kpc) {
   using Cfg = ClCfg<T>;
@@ -328,11 +328,18 @@ __global__ void __launch_bounds__(kClThreads, 2) decode_cluster_kernel(DecodePar
   const int tid = threadIdx.x, warp = tid / 32, lane = tid % 32;
   const int rank = S > 1 ? static_cast<int>(cluster_ctarank()) : 0;
   const int row = blockIdx.x / S;
-  const int k0 = min(p.kv_len, rank * kpc);
-  const int k1 = min(p.kv_len, k0 + kpc);
-  const int nch = (k1 - k0 + KS - 1) / KS;
   if (S > 1) cluster_arrive_relaxed();  // paired with the wait before the merge
   griddep_launch_dependents();
+  int len = p.kv_len, kp = kpc;
+  if constexpr (PAGED) {
+    // The lengths (and tables) may come from the preceding kernel (an append).
+    griddep_wait();
+    len = min(max(__ldcg(p.seq_lens + row / p.heads), 0), p.max_pages * kPageKeys);
+    kp = ((len + S - 1) / S + kPageKeys - 1) / kPageKeys * kPageKeys;  // page-aligned ranges
+  }
+  const int k0 = min(len, rank * kp);
+  const int k1 = min(len, k0 + kp);
+  const int nch = (k1 - k0 + KS - 1) / KS;
 
   if (tid == 0) {
     for (int i = 0; i < kClStages; ++i) {
@@ -344,7 +351,7 @@ __global__ void __launch_bounds__(kClThreads, 2) decode_cluster_kernel(DecodePar
   }
   __syncthreads();
 
-  const size_t base = (static_cast<size_t>(row) * p.cap + k0) * 64;
+  const size_t base = PAGED ? 0 : (static_cast<size_t>(row) * p.cap + k0) * 64;
   if (warp == kClWarps) {
     // Producer: all of the range's stages at once, then refills as warps free them.
     if (!p.kv_stable) griddep_wait();
@@ -357,11 +364,27 @@ __global__ void __launch_bounds__(kClThreads, 2) decode_cluster_kernel(DecodePar
           break;
         const int n = min(KS, k1 - k0 - c * KS);
         const uint32_t bytes = static_cast<uint32_t>(n) * 64 * sizeof(T);
-        mbar_arrive_expect_tx(&full[st], 2 * bytes);
-        bulk_load(kbuf + st * KS * 64, static_cast<const T*>(p.k) + base + c * KS * 64, bytes,
-                  &full[st]);
-        bulk_load(vbuf + st * KS * 64, static_cast<const T*>(p.v) + base + c * KS * 64, bytes,
-                  &full[st]);
+        size_t off = base + static_cast<size_t>(c) * KS * 64;
+        bool ok_src = true;
+        if constexpr (PAGED) {
+          // A stage never crosses a page: ranges start on page boundaries and
+          // KS divides kPageKeys.
+          const int j0 = k0 + c * KS;
+          const int page = __ldcg(p.block_table +
+                                  static_cast<size_t>(row / p.heads) * p.max_pages +
+                                  j0 / kPageKeys);
+          ok_src = page >= 0 && page < p.num_pages;
+          off = ((static_cast<size_t>(page) * p.heads + row % p.heads) * kPageKeys +
+                 j0 % kPageKeys) * 64;
+        }
+        if (ok_src) {
+          mbar_arrive_expect_tx(&full[st], 2 * bytes);
+          bulk_load(kbuf + st * KS * 64, static_cast<const T*>(p.k) + off, bytes, &full[st]);
+          bulk_load(vbuf + st * KS * 64, static_cast<const T*>(p.v) + off, bytes, &full[st]);
+        } else {  // bad page id: flag it, copy nothing, let the stage complete
+          if (p.err) atomicOr(p.err, kErrBadArgs);
+          mbar_arrive(&full[st]);
+        }
         ++issued;
       }
       if (s_abort) {
@@ -497,7 +520,7 @@ __global__ void __launch_bounds__(kClThreads, 2) decode_cluster_kernel(DecodePar
     }
   }
   if (tid < 64) {
-    const float val = O / L;
+    const float val = L > 0.f ? O / L : 0.f;  // a paged row with no keys gives zeros
     if (p.out_dtype == 0)
       static_cast<float*>(p.out)[static_cast<size_t>(row) * 64 + tid] = val;
     else
@@ -523,7 +546,7 @@ cudaError_t launch_ch(const DecodeParams& p, cudaStream_t s) {
   return launch_t<T, 128>(p, s);
 }
 
-template <typename T>
+template <typename T, bool PAGED>
 cudaError_t launch_cluster_t(const DecodeParams& p, int S, int kpc, cudaStream_t s) {
   const size_t smem = ClCfg<T>::kSmem;
   int dev = 0;
@@ -532,8 +555,8 @@ cudaError_t launch_cluster_t(const DecodeParams& p, int S, int kpc, cudaStream_t
   static bool configured[64] = {};
   if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
   if (!configured[dev]) {
-    e = cudaFuncSetAttribute(decode_cluster_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             static_cast<int>(smem));
+    e = cudaFuncSetAttribute(decode_cluster_kernel<T, PAGED>,
+                             cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
     if (e != cudaSuccess) return e;
     configured[dev] = true;
   }
@@ -551,7 +574,7 @@ cudaError_t launch_cluster_t(const DecodeParams& p, int S, int kpc, cudaStream_t
   attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 2;
-  e = cudaLaunchKernelEx(&cfg, decode_cluster_kernel<T>, p, S, kpc);
+  e = cudaLaunchKernelEx(&cfg, decode_cluster_kernel<T, PAGED>, p, S, kpc);
   if (e != cudaSuccess) return e;
   return cudaGetLastError();
 }
@@ -563,13 +586,112 @@ cudaError_t launch_decode_cluster(const DecodeParams& p, int splits, int keys_pe
   if (splits < 1 || splits > kDecodeMaxCluster) return cudaErrorInvalidValue;
   switch (p.kv_dtype) {
     case 0:
-      return launch_cluster_t<float>(p, splits, keys_per_cta, s);
+      return launch_cluster_t<float, false>(p, splits, keys_per_cta, s);
     case 1:
-      return launch_cluster_t<__nv_bfloat16>(p, splits, keys_per_cta, s);
+      return launch_cluster_t<__nv_bfloat16, false>(p, splits, keys_per_cta, s);
     case 2:
-      return launch_cluster_t<__half>(p, splits, keys_per_cta, s);
+      return launch_cluster_t<__half, false>(p, splits, keys_per_cta, s);
   }
   return cudaErrorInvalidValue;
+}
+
+cudaError_t launch_decode_paged(const DecodeParams& p, int splits, cudaStream_t s) {
+  if (splits < 1 || splits > kDecodeMaxCluster) return cudaErrorInvalidValue;
+  switch (p.kv_dtype) {
+    case 0:
+      return launch_cluster_t<float, true>(p, splits, 0, s);
+    case 1:
+      return launch_cluster_t<__nv_bfloat16, true>(p, splits, 0, s);
+    case 2:
+      return launch_cluster_t<__half, true>(p, splits, 0, s);
+  }
+  return cudaErrorInvalidValue;
+}
+
+namespace {
+
+// One CTA per sequence: writes its heads' new key and value rows at the
+// sequence's current length, then advances the length.
+template <typename T>
+__global__ void kv_append_kernel(DecodeParams p, const T* k_new, const T* v_new) {
+  const int b = blockIdx.x;
+  __shared__ int s_pos, s_page;
+  if (threadIdx.x == 0) {
+    s_pos = p.seq_lens[b];
+    const int slot = s_pos / kPageKeys;
+    s_page = (s_pos >= 0 && slot < p.max_pages)
+                 ? p.block_table[static_cast<size_t>(b) * p.max_pages + slot]
+                 : -1;
+    if (s_page < 0 || s_page >= p.num_pages) {
+      if (p.err) atomicOr(p.err, kErrBadArgs);
+      s_page = -1;
+    }
+  }
+  __syncthreads();
+  if (s_page < 0) return;
+  const int pos = s_pos;
+  T* kd = static_cast<T*>(const_cast<void*>(p.k));
+  T* vd = static_cast<T*>(const_cast<void*>(p.v));
+  for (int i = threadIdx.x; i < p.heads * 64; i += blockDim.x) {
+    const int h = i / 64, d = i % 64;
+    const size_t dst =
+        ((static_cast<size_t>(s_page) * p.heads + h) * kPageKeys + pos % kPageKeys) * 64 + d;
+    const size_t src = (static_cast<size_t>(b) * p.heads + h) * 64 + d;
+    kd[dst] = k_new[src];
+    vd[dst] = v_new[src];
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) const_cast<int*>(p.seq_lens)[b] = pos + 1;
+}
+
+// Block i copies page src[i] to page dst[i] in both pools, 16 bytes a thread.
+__global__ void kv_copy_pages_kernel(DecodeParams p, const int* src, const int* dst,
+                                     size_t page_bytes) {
+  const int a = src[blockIdx.x], b = dst[blockIdx.x];
+  if (a < 0 || a >= p.num_pages || b < 0 || b >= p.num_pages) {
+    if (threadIdx.x == 0 && p.err) atomicOr(p.err, kErrBadArgs);
+    return;
+  }
+  const uint4* ks = reinterpret_cast<const uint4*>(static_cast<const uint8_t*>(p.k) + a * page_bytes);
+  const uint4* vs = reinterpret_cast<const uint4*>(static_cast<const uint8_t*>(p.v) + a * page_bytes);
+  uint4* kd = reinterpret_cast<uint4*>(static_cast<uint8_t*>(const_cast<void*>(p.k)) + b * page_bytes);
+  uint4* vd = reinterpret_cast<uint4*>(static_cast<uint8_t*>(const_cast<void*>(p.v)) + b * page_bytes);
+  for (size_t i = threadIdx.x; i < page_bytes / 16; i += blockDim.x) {
+    kd[i] = ks[i];
+    vd[i] = vs[i];
+  }
+}
+
+}  // namespace
+
+cudaError_t launch_kv_append(const DecodeParams& p, int batch, const void* k_new,
+                             const void* v_new, cudaStream_t s) {
+  switch (p.kv_dtype) {
+    case 0:
+      kv_append_kernel<float><<<batch, 256, 0, s>>>(p, static_cast<const float*>(k_new),
+                                                    static_cast<const float*>(v_new));
+      break;
+    case 1:
+      kv_append_kernel<__nv_bfloat16><<<batch, 256, 0, s>>>(
+          p, static_cast<const __nv_bfloat16*>(k_new), static_cast<const __nv_bfloat16*>(v_new));
+      break;
+    case 2:
+      kv_append_kernel<__half><<<batch, 256, 0, s>>>(p, static_cast<const __half*>(k_new),
+                                                     static_cast<const __half*>(v_new));
+      break;
+    default:
+      return cudaErrorInvalidValue;
+  }
+  return cudaGetLastError();
+}
+
+cudaError_t launch_kv_copy_pages(const DecodeParams& p, const int* src, const int* dst, int n,
+                                 cudaStream_t s) {
+  if (n <= 0) return cudaSuccess;
+  const size_t elem = p.kv_dtype == 0 ? 4 : 2;
+  const size_t page_bytes = static_cast<size_t>(p.heads) * kPageKeys * 64 * elem;
+  kv_copy_pages_kernel<<<n, 256, 0, s>>>(p, src, dst, page_bytes);
+  return cudaGetLastError();
 }
 
 cudaError_t launch_decode(const DecodeParams& p, cudaStream_t s) {

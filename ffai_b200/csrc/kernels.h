@@ -8,6 +8,16 @@
 
 namespace ffai {
 
+// Error bits written to the context's device error word.
+enum : unsigned {
+  kErrTimeoutProducer = 1u << 0,
+  kErrTimeoutMma = 1u << 1,
+  kErrTimeoutSoftmax = 1u << 2,
+  kErrTimeoutDrain = 1u << 3,
+  kErrTimeoutConsumer = 1u << 4,
+  kErrBadArgs = 1u << 8,
+};
+
 // ---- decode (decode.cu) ----------------------------------------------------
 
 constexpr int kPartStride = 66;  // per (row, split): m, l, o[64]
@@ -30,7 +40,16 @@ struct DecodeParams {
   float scale_log2;
   unsigned* err;  // device error word (bounded waits of the cluster kernel)
   int kv_stable;  // cluster kernel: copy K/V before the programmatic-dependency wait
+  // paged caches (launch_decode_paged): k, v are pools of pages of kPageKeys
+  // keys, (num_pages, heads, kPageKeys, 64); row = b * heads + h
+  const int* block_table;  // (batch, max_pages) page ids
+  const int* seq_lens;     // (batch) live keys per sequence
+  int max_pages;
+  int num_pages;
+  int heads;
 };
+
+constexpr int kPageKeys = 64;
 
 cudaError_t launch_decode(const DecodeParams& p, cudaStream_t s);
 
@@ -41,6 +60,19 @@ cudaError_t launch_decode(const DecodeParams& p, cudaStream_t s);
 constexpr int kDecodeMaxCluster = 8;
 cudaError_t launch_decode_cluster(const DecodeParams& p, int splits, int keys_per_cta,
                                   cudaStream_t s);
+// The cluster kernel over a paged cache: each sequence's live length comes
+// from p.seq_lens (read on the device, after the preceding kernel), split
+// into page-aligned ranges over `splits` CTAs.  Rows with no keys get zeros.
+cudaError_t launch_decode_paged(const DecodeParams& p, int splits, cudaStream_t s);
+// Append one key and value per (sequence, head) at position seq_lens[b]
+// (page block_table[b][pos / kPageKeys]) and advance seq_lens[b].
+// k_new, v_new: (batch, heads, 64) of the cache type.
+cudaError_t launch_kv_append(const DecodeParams& p, int batch, const void* k_new,
+                             const void* v_new, cudaStream_t s);
+// Copy whole pages src[i] -> dst[i] of both pools (a beam taking over a
+// partly filled page before appending to it).
+cudaError_t launch_kv_copy_pages(const DecodeParams& p, const int* src, const int* dst, int n,
+                                 cudaStream_t s);
 
 // ---- checked f32 prefill (prefill_simt.cu) ---------------------------------
 

@@ -165,6 +165,45 @@ int ffai_attn_decode(ffai_attn_ctx* ctx, const ffai_attn_desc* d, const void* q,
 int ffai_attn_decode_static(const ffai_attn_desc* d, const void* q, const void* k, const void* v,
                             void* o, float* lse, int32_t num_splits, void* stream);
 
+/* ---- paged KV cache ------------------------------------------------------
+ * A device-resident cache that grows in place, replacing the reference's
+ * per-step Tensor::cat of the decoder self-attention cache and its per-step
+ * split / transpose / contiguous copies (DecoderState, text_decoder.rs:
+ * 1226-1243; growth at :657-664; re-layout at :841), and letting beams share
+ * pages instead of cloning caches (TextDecoder::save/restore, :1363-1381).
+ * Pools k_pool, v_pool hold num_pages pages of FFAI_PAGE_KEYS keys for every
+ * head: (num_pages, heads, FFAI_PAGE_KEYS, 64) of d->kv_dtype.  Sequence b
+ * (a beam) owns pages block_table[b * max_pages + i] for its keys
+ * [i * FFAI_PAGE_KEYS, (i + 1) * FFAI_PAGE_KEYS) and has seq_lens[b] live
+ * keys; block_table and seq_lens are DEVICE int32 arrays.  The host owns the
+ * page allocation (a page must be in the table before a key lands in it). */
+#define FFAI_PAGE_KEYS 64
+
+/* Decode over a paged cache: q (batch, heads, 1, 64) against each
+ * sequence's seq_lens[b] keys (read on the device, so an append queued just
+ * before on the stream is seen).  d->kv_len, when > 0, bounds the lengths for
+ * the work split.  Rows with no keys give zeros.  Page ids outside
+ * [0, num_pages) are not read; ffai_attn_sync then reports
+ * FFAI_ATTN_ERR_INVALID. */
+int ffai_attn_decode_paged(ffai_attn_ctx* ctx, const ffai_attn_desc* d, const void* q,
+                           const void* k_pool, const void* v_pool, int32_t num_pages,
+                           const int32_t* block_table, const int32_t* seq_lens, int32_t max_pages,
+                           void* o, float* lse, void* stream);
+
+/* Append one key and value per (sequence, head): k_new, v_new (batch, heads,
+ * 64) of d->kv_dtype land at position seq_lens[b], which then advances by 1
+ * (in place; the reference concatenates a new tensor each step). */
+int ffai_kv_append(ffai_attn_ctx* ctx, const ffai_attn_desc* d, void* k_pool, void* v_pool,
+                   int32_t num_pages, const int32_t* block_table, int32_t* seq_lens,
+                   int32_t max_pages, const void* k_new, const void* v_new, void* stream);
+
+/* Copy whole pages src_pages[i] -> dst_pages[i] (device int32 lists) in both
+ * pools: a beam that forks from another takes its own copy of the shared,
+ * partly filled last page before appending to it. */
+int ffai_kv_copy_pages(ffai_attn_ctx* ctx, const ffai_attn_desc* d, void* k_pool, void* v_pool,
+                       int32_t num_pages, const int32_t* src_pages, const int32_t* dst_pages,
+                       int32_t n, void* stream);
+
 /* Variable-length (ragged) prefill over packed segments, TOKEN_MAJOR
  * (T, H, 64) operands and output.  Segment s owns query rows
  * [cu_seqlens_q[s], cu_seqlens_q[s+1]) and keys [cu_seqlens_k[s],
