@@ -51,6 +51,7 @@ class Desc(ctypes.Structure):
         ("q_offset", ctypes.c_int32),
         ("scale", ctypes.c_float),
         ("flags", ctypes.c_uint32),
+        ("token_stride", ctypes.c_int32),
     ]
 
 

@@ -91,6 +91,33 @@ def _dims(t: torch.Tensor, layout: str):
     raise ValueError(layout)
 
 
+def _token_stride(t: torch.Tensor):
+    """Elements between tokens of a token-major (..., N, H, 64) view whose
+    heads and head dims are dense (0 for a contiguous tensor), or None when
+    the view has some other shape of strides."""
+    if t.is_contiguous():
+        return 0
+    if t.stride(-1) != 1 or t.stride(-2) != 64:
+        return None
+    ts = t.stride(-3)
+    if t.dim() == 4 and t.shape[0] > 1 and t.stride(0) != t.shape[1] * ts:
+        return None
+    return ts
+
+
+def _operands(tensors, layouts):
+    """Operands and their shared token stride: token-major views of one
+    buffer with one stride (e.g. the three thirds of a fused QKV projection
+    output) are passed as they are; anything else non-contiguous is copied."""
+    strides = {_token_stride(t) for t, lay in zip(tensors, layouts) if lay == "token"}
+    ts = 0
+    if len(strides) == 1 and None not in strides:
+        ts = strides.pop()
+    out = [t if (lay == "token" and ts) or t.is_contiguous() else t.contiguous()
+           for t, lay in zip(tensors, layouts)]
+    return out, ts
+
+
 def prefill(q, k, v, *, scale: float = 1.0, q_layout="heads", k_layout="heads",
             v_layout="heads", out_layout="heads", out_dtype=torch.float32, kv_len=None,
             with_lse=False, checked=False, causal=False, q_offset=0, out=None):
@@ -103,6 +130,7 @@ def prefill(q, k, v, *, scale: float = 1.0, q_layout="heads", k_layout="heads",
     B, H, Nq = _dims(q, q_layout)
     _, _, cap = _dims(k, k_layout)
     Nk = cap if kv_len is None else kv_len
+    (q, k, v), ts = _operands((q, k, v), (q_layout, k_layout, v_layout))
     if out is None:
         shape = (B, H, Nq, 64) if out_layout == "heads" else (B, Nq, H, 64)
         out = torch.empty(shape, dtype=out_dtype, device=dev)
@@ -115,7 +143,7 @@ def prefill(q, k, v, *, scale: float = 1.0, q_layout="heads", k_layout="heads",
                       q_layout=_LAYOUT[q_layout], k_layout=_LAYOUT[k_layout],
                       v_layout=_LAYOUT[v_layout], out_layout=_LAYOUT[out_layout],
                       causal=int(causal), q_offset=q_offset, scale=scale,
-                      flags=_abi.FLAG_CHECKED_F32 if checked else 0)
+                      flags=_abi.FLAG_CHECKED_F32 if checked else 0, token_stride=ts)
     ctx = context(dev.index)
     st = _abi.load().ffai_attn_prefill(ctx, ctypes.byref(d), _ptr(q), _ptr(k), _ptr(v), _ptr(out),
                                        _ptr(lse), _stream(dev))
@@ -184,6 +212,7 @@ def varlen(q, k, v, cu_seqlens_q, cu_seqlens_k=None, *, scale: float = 1.0,
     if q.dim() != 3 or q.shape[-1] != 64:
         raise ValueError("varlen operands are (T, H, 64)")
     T, H = q.shape[0], q.shape[1]
+    (q, k, v), ts = _operands((q, k, v), ("token", "token", "token"))
     cq = [int(x) for x in cu_seqlens_q]
     ck = cq if cu_seqlens_k is None else [int(x) for x in cu_seqlens_k]
     n_seg = len(cq) - 1
@@ -195,7 +224,7 @@ def varlen(q, k, v, cu_seqlens_q, cu_seqlens_k=None, *, scale: float = 1.0,
     d = _abi.new_desc(heads=H, q_dtype=_DT[q.dtype], kv_dtype=_DT[k.dtype],
                       out_dtype=_DT[out.dtype], q_layout=_abi.LAYOUT_TOKEN_MAJOR,
                       k_layout=_abi.LAYOUT_TOKEN_MAJOR, v_layout=_abi.LAYOUT_TOKEN_MAJOR,
-                      out_layout=_abi.LAYOUT_TOKEN_MAJOR, scale=scale)
+                      out_layout=_abi.LAYOUT_TOKEN_MAJOR, scale=scale, token_stride=ts)
     ctx = context(dev.index)
     st = _abi.load().ffai_attn_varlen(ctx, ctypes.byref(d), arr_q, arr_k, n_seg, _ptr(q), _ptr(k),
                                       _ptr(v), _ptr(out), _ptr(lse), _stream(dev))

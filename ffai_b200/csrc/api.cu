@@ -183,6 +183,11 @@ int check_desc(const ffai_attn_ctx* ctx, const ffai_attn_desc* d, int op) {
     return set_error(ctx, FFAI_ATTN_DECLINED, "out_dtype %d: f32 or bf16 only", d->out_dtype);
   if (!(d->scale > 0.f) || !std::isfinite(d->scale))
     return set_error(ctx, FFAI_ATTN_ERR_INVALID, "scale must be finite and > 0");
+  if (d->token_stride != 0 &&
+      (d->token_stride < d->heads * kHD || d->token_stride % 8 != 0))
+    return set_error(ctx, FFAI_ATTN_ERR_INVALID,
+                     "token_stride %d: 0, or a multiple of 8 of at least heads * 64",
+                     d->token_stride);
   if (op == FFAI_OP_VARLEN) {
     if (d->q_layout != FFAI_LAYOUT_TOKEN_MAJOR || d->k_layout != FFAI_LAYOUT_TOKEN_MAJOR ||
         d->v_layout != FFAI_LAYOUT_TOKEN_MAJOR || d->out_layout != FFAI_LAYOUT_TOKEN_MAJOR)
@@ -229,14 +234,16 @@ int check_desc(const ffai_attn_ctx* ctx, const ffai_attn_desc* d, int op) {
 }
 
 // Element strides (b, h, row, d) of an operand of `rows` rows per head.
-Strides strides_of(int layout, int H, long long rows) {
+// token_stride: elements between tokens of a TOKEN_MAJOR operand (0: dense).
+Strides strides_of(int layout, int H, long long rows, long long token_stride = 0) {
   Strides s{};
+  const long long ts = token_stride > 0 ? token_stride : static_cast<long long>(H) * kHD;
   switch (layout) {
     case FFAI_LAYOUT_HEADS_SPLIT:
       s = {H * rows * kHD, rows * kHD, kHD, 1};
       break;
     case FFAI_LAYOUT_TOKEN_MAJOR:
-      s = {rows * H * kHD, kHD, static_cast<long long>(H) * kHD, 1};
+      s = {rows * ts, kHD, ts, 1};
       break;
     case FFAI_LAYOUT_KT:
       s = {H * rows * kHD, rows * kHD, 1, rows};
@@ -257,7 +264,7 @@ void init_encoder() {
 // 3-d bf16/f16 tensor map over 64-element (128-byte) rows with a box of 128
 // rows and 128-byte swizzle.  token_major: dims {64, H, T}; else {64, rows, B*H}.
 int make_map(ffai_attn_ctx* ctx, CUtensorMap* map, const void* base, bool token_major, int H,
-             long long rows_or_tokens, long long groups) {
+             long long rows_or_tokens, long long groups, long long token_stride = 0) {
   if (!g_encode) return set_error(ctx, FFAI_ATTN_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
   if (reinterpret_cast<uintptr_t>(base) % 16 != 0)
     return set_error(ctx, FFAI_ATTN_ERR_INVALID, "operand base address not 16-byte aligned");
@@ -270,7 +277,7 @@ int make_map(ffai_attn_ctx* ctx, CUtensorMap* map, const void* base, bool token_
     dims[1] = static_cast<cuuint64_t>(H);
     dims[2] = static_cast<cuuint64_t>(rows_or_tokens);
     strides[0] = kHD * 2;
-    strides[1] = static_cast<cuuint64_t>(H) * kHD * 2;
+    strides[1] = static_cast<cuuint64_t>(token_stride > 0 ? token_stride : H * kHD) * 2;
     box[0] = kHD;
     box[1] = 1;
     box[2] = kTcRows;
@@ -387,6 +394,7 @@ struct Operand {
   bool token_major;
   long long rows;
   long long groups;
+  long long token_stride = 0;  // token-major: elements between tokens (0: dense)
 };
 
 int run_tc(ffai_attn_ctx* ctx, const Operand& q, const Operand& k, const Operand& v, int H,
@@ -395,11 +403,11 @@ int run_tc(ffai_attn_ctx* ctx, const Operand& q, const Operand& k, const Operand
   if (reinterpret_cast<uintptr_t>(o) % 8 != 0)
     return set_error(ctx, FFAI_ATTN_ERR_INVALID, "prefill output must be 8-byte aligned");
   CUtensorMap tq, tk, tv;
-  int st = make_map(ctx, &tq, q.ptr, q.token_major, H, q.rows, q.groups);
+  int st = make_map(ctx, &tq, q.ptr, q.token_major, H, q.rows, q.groups, q.token_stride);
   if (st) return st;
-  st = make_map(ctx, &tk, k.ptr, k.token_major, H, k.rows, k.groups);
+  st = make_map(ctx, &tk, k.ptr, k.token_major, H, k.rows, k.groups, k.token_stride);
   if (st) return st;
-  st = make_map(ctx, &tv, v.ptr, v.token_major, H, v.rows, v.groups);
+  st = make_map(ctx, &tv, v.ptr, v.token_major, H, v.rows, v.groups, v.token_stride);
   if (st) return st;
   TcParams p{};
   p.units = ctx->d_units;
@@ -441,9 +449,9 @@ int prefill_impl(ffai_attn_ctx* ctx, const ffai_attn_desc* d, const void* q, con
     p.v = static_cast<const float*>(v);
     p.out = o;
     p.lse = lse;
-    p.qs = strides_of(d->q_layout, H, Nq);
-    p.ks = strides_of(d->k_layout, H, cap);
-    p.vs = strides_of(d->v_layout, H, cap);
+    p.qs = strides_of(d->q_layout, H, Nq, d->token_stride);
+    p.ks = strides_of(d->k_layout, H, cap, d->token_stride);
+    p.vs = strides_of(d->v_layout, H, cap, d->token_stride);
     p.os = strides_of(d->out_layout, H, Nq);
     if (out_tm) {
       p.lse_sb = Nq;
@@ -486,14 +494,16 @@ int prefill_impl(ffai_attn_ctx* ctx, const ffai_attn_desc* d, const void* q, con
     if (st) return st;
     uint16_t* base = static_cast<uint16_t*>(ctx->d_stage);
     if (stage_q) {
-      FFAI_CUDA(ctx, launch_to_16bit_heads_split(q, d->q_dtype, strides_of(d->q_layout, H, Nq), B,
+      FFAI_CUDA(ctx, launch_to_16bit_heads_split(q, d->q_dtype,
+                                                 strides_of(d->q_layout, H, Nq, d->token_stride), B,
                                                  H, Nq, base, dt16 == FFAI_DT_F16, s));
       qq = base;
       q_tm = false;
       base += q_elems;
     }
     if (stage_k) {
-      FFAI_CUDA(ctx, launch_to_16bit_heads_split(k, d->kv_dtype, strides_of(d->k_layout, H, cap), B,
+      FFAI_CUDA(ctx, launch_to_16bit_heads_split(k, d->kv_dtype,
+                                                 strides_of(d->k_layout, H, cap, d->token_stride), B,
                                                  H, Nk, base, dt16 == FFAI_DT_F16, s));
       kk = base;
       k_tm = false;
@@ -501,7 +511,8 @@ int prefill_impl(ffai_attn_ctx* ctx, const ffai_attn_desc* d, const void* q, con
       base += kv_elems;
     }
     if (stage_v) {
-      FFAI_CUDA(ctx, launch_to_16bit_heads_split(v, d->kv_dtype, strides_of(d->v_layout, H, cap), B,
+      FFAI_CUDA(ctx, launch_to_16bit_heads_split(v, d->kv_dtype,
+                                                 strides_of(d->v_layout, H, cap, d->token_stride), B,
                                                  H, Nk, base, dt16 == FFAI_DT_F16, s));
       vv = base;
       v_tm = false;
@@ -518,9 +529,9 @@ int prefill_impl(ffai_attn_ctx* ctx, const ffai_attn_desc* d, const void* q, con
   int st = prepare_work(ctx, qs, ql, ks, kl, H, s, d->causal, d->q_offset);
   if (st) return st;
   const long long BH = static_cast<long long>(B) * H;
-  Operand oq{qq, q_tm, q_tm ? static_cast<long long>(B) * Nq : Nq, BH};
-  Operand ok{kk, k_tm, k_tm ? static_cast<long long>(B) * kcap : kcap, BH};
-  Operand ov{vv, v_tm, v_tm ? static_cast<long long>(B) * vcap : vcap, BH};
+  Operand oq{qq, q_tm, q_tm ? static_cast<long long>(B) * Nq : Nq, BH, d->token_stride};
+  Operand ok{kk, k_tm, k_tm ? static_cast<long long>(B) * kcap : kcap, BH, d->token_stride};
+  Operand ov{vv, v_tm, v_tm ? static_cast<long long>(B) * vcap : vcap, BH, d->token_stride};
   return run_tc(ctx, oq, ok, ov, H, ab_f16, o, d->out_dtype == FFAI_DT_BF16,
                 d->out_layout == FFAI_LAYOUT_TOKEN_MAJOR, Nq, lse, static_cast<long long>(B) * Nq,
                 d->scale, s, d->causal, d->q_offset);
@@ -806,7 +817,8 @@ int ffai_attn_varlen(ffai_attn_ctx* ctx, const ffai_attn_desc* d, const int32_t*
   st = prepare_work(ctx, qs, ql, ks, kl, d->heads, s);
   if (st) return st;
   if (Tq == 0) return FFAI_ATTN_OK;
-  const Operand oq{q, true, Tq, 1}, ok{k, true, Tk, 1}, ov{v, true, Tk, 1};
+  const Operand oq{q, true, Tq, 1, d->token_stride}, ok{k, true, Tk, 1, d->token_stride},
+      ov{v, true, Tk, 1, d->token_stride};
   return run_tc(ctx, oq, ok, ov, d->heads, d->q_dtype == FFAI_DT_F16, o,
                 d->out_dtype == FFAI_DT_BF16, true, 0, lse, Tq, d->scale, s);
 }
@@ -817,6 +829,8 @@ int ffai_attn_prefill_host(ffai_attn_ctx* ctx, const ffai_attn_desc* d, const vo
   int st = check_desc(ctx, d, FFAI_OP_PREFILL);
   if (st) return st;
   if (!q || !k || !v || !o) return set_error(ctx, FFAI_ATTN_ERR_INVALID, "null operand");
+  if (d->token_stride != 0)
+    return set_error(ctx, FFAI_ATTN_DECLINED, "host prefill: dense operands only (token_stride 0)");
   DeviceGuard g(ctx->device);
   if (!ctx->s_h2d) {
     FFAI_CUDA(ctx, cudaStreamCreateWithFlags(&ctx->s_h2d, cudaStreamNonBlocking));
@@ -978,6 +992,8 @@ int ffai_attn_multi_prefill_host(ffai_attn_ctx* const* ctxs, int32_t n_ctx,
   int st = check_desc(nullptr, d, FFAI_OP_PREFILL);
   if (st) return st;
   if (!q || !k || !v || !o) return set_error(nullptr, FFAI_ATTN_ERR_INVALID, "null operand");
+  if (d->token_stride != 0)
+    return set_error(nullptr, FFAI_ATTN_DECLINED, "host prefill: dense operands only");
   if (lse && d->out_layout == FFAI_LAYOUT_TOKEN_MAJOR)
     return set_error(nullptr, FFAI_ATTN_DECLINED, "host prefill: lse needs heads-split output");
   const int B = d->batch, H = d->heads, Nq = d->q_len;

@@ -97,6 +97,13 @@ typedef struct ffai_attn_desc {
   float scale;         /* logits = scale * q.k; the reference folds it into
                           q before the kernel, so its callers pass 1.0      */
   uint32_t flags;      /* FFAI_ATTN_FLAG_*                                  */
+  int32_t token_stride; /* TOKEN_MAJOR q/k/v inputs: elements from one token's
+                          row to the next; 0 means heads * 64 (dense).  With
+                          3 * heads * 64, q, k and v can be the three views of
+                          one fused QKV projection output (T, 3, heads, 64),
+                          read in place with no head split (the reference's
+                          prep glue, text_decoder.rs:1083-1124).  A multiple
+                          of 8.  Not for the host-buffer entries.          */
 } ffai_attn_desc;
 
 typedef struct ffai_attn_ctx ffai_attn_ctx;

@@ -266,3 +266,33 @@ def test_varlen_matches_batched():
     pack = lambda t: t.transpose(1, 2).reshape(3 * 384, 4, 64).contiguous()
     b = attention.varlen(pack(qd), pack(kd), pack(vd), [0, 384, 768, 1152], scale=S)
     assert torch.equal(pack(a), b)
+
+
+@pytest.mark.parametrize("dtype,checked", [(torch.bfloat16, False), (torch.float32, False),
+                                           (torch.float32, True)])
+def test_fused_qkv_views_read_in_place(dtype, checked):
+    """q, k, v as the three thirds of one fused projection output
+    (B, N, 3, H, 64): read with a token stride of 3*H*64, no copies; equal to
+    the result on dense copies."""
+    B, N, H = 2, 300, 8
+    g = torch.Generator().manual_seed(50)
+    qkv = (torch.randn(B, N, 3, H, 64, generator=g) * 0.5).to(dtype).to(DEV)
+    q, k, v = qkv[:, :, 0], qkv[:, :, 1], qkv[:, :, 2]
+    assert not q.is_contiguous()
+    kw = dict(scale=S, q_layout="token", k_layout="token", v_layout="token", out_layout="token",
+              out_dtype=torch.bfloat16, checked=checked)
+    got = attention.prefill(q, k, v, **kw)
+    ref = attention.prefill(q.contiguous(), k.contiguous(), v.contiguous(), **kw)
+    assert torch.equal(got, ref)
+
+
+def test_fused_qkv_views_varlen():
+    g = torch.Generator().manual_seed(51)
+    lens = [200, 333, 129]
+    T, H = sum(lens), 4
+    qkv = (torch.randn(T, 3, H, 64, generator=g) * 0.5).to(torch.bfloat16).to(DEV)
+    cu = [0, 200, 533, 662]
+    got = attention.varlen(qkv[:, 0], qkv[:, 1], qkv[:, 2], cu, scale=S)
+    ref = attention.varlen(qkv[:, 0].contiguous(), qkv[:, 1].contiguous(),
+                           qkv[:, 2].contiguous(), cu, scale=S)
+    assert torch.equal(got, ref)
