@@ -272,12 +272,67 @@ def bench_decode(steps: int):
         t_graph = a.elapsed_time(b) / 1e3 / (steps * layers)
         del g
         res[name] = {"rows": rows, "keys": keys, "layers_per_pass": layers, "kv_stable": stable,
+                     "kernel": "decode_cluster_kernel",
                      "bytes_per_launch": bytes_per,
                      "us_per_launch": round(t_launch * 1e6, 2),
                      "gbs": round(bytes_per / t_launch / 1e9, 1),
                      "us_per_launch_graph": round(t_graph * 1e6, 2),
                      "gbs_graph": round(bytes_per / t_graph / 1e9, 1)}
+    res["self_448_paged"] = bench_decode_paged(steps, dev)
     return res
+
+
+def bench_decode_paged(steps: int, dev):
+    """The self-attention shape (5 beams x 12 heads x 448 keys, bf16) from a
+    paged cache: 64-key pages scattered over the pool, one table per layer."""
+    import torch
+
+    from ffai_b200 import kvcache, workloads
+    beams, heads, keys, layers = workloads.C3_BEAMS, workloads.C3_HEADS, 448, 24
+    per = (keys + 63) // 64
+    g = torch.Generator().manual_seed(5)
+    pools, tables = [], []
+    for _ in range(layers):
+        n = beams * per
+        pools.append((torch.randn(n, heads, 64, 64, device=dev).to(torch.bfloat16),
+                       torch.randn(n, heads, 64, 64, device=dev).to(torch.bfloat16)))
+        tables.append(torch.randperm(n, generator=g).view(beams, per).to(torch.int32).to(dev))
+    lens = torch.full((beams,), keys, dtype=torch.int32, device=dev)
+    q = torch.randn(beams, heads, 1, 64, device=dev) * 0.5
+    outs = [torch.empty(beams, heads, 1, 64, device=dev) for _ in range(layers)]
+
+    def one_pass():
+        for (kp, vp), tb, o in zip(pools, tables, outs):
+            kvcache.decode_paged(q, kp, vp, tb, lens, out=o, kv_bound=keys)
+
+    for _ in range(3):
+        one_pass()
+    torch.cuda.synchronize()
+    gr = torch.cuda.CUDAGraph()
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        one_pass()
+        torch.cuda.synchronize()
+        with torch.cuda.graph(gr, stream=s):
+            one_pass()
+    torch.cuda.current_stream().wait_stream(s)
+    for _ in range(3):
+        gr.replay()
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(steps):
+        gr.replay()
+    b.record()
+    torch.cuda.synchronize()
+    t = a.elapsed_time(b) / 1e3 / (steps * layers)
+    del gr
+    rows = beams * heads
+    bytes_per = rows * (2 * keys * 64 * 2) + rows * 64 * (4 + 4)
+    return {"rows": rows, "keys": keys, "layers_per_pass": layers, "page_keys": 64,
+            "kernel": "decode_cluster_kernel (paged)", "bytes_per_launch": bytes_per,
+            "us_per_launch_graph": round(t * 1e6, 2), "gbs_graph": round(bytes_per / t / 1e9, 1)}
 
 
 def bench_ragged(dist, steps: int, peaks):

@@ -64,14 +64,16 @@ def _stream(dev: torch.device):
     return ctypes.c_void_p(torch.cuda.current_stream(dev).cuda_stream)
 
 
-def _need_cuda(*ts: torch.Tensor) -> torch.device:
+def _need_cuda(*ts: torch.Tensor, strided: bool = False) -> torch.device:
+    """The operands' common CUDA device; they must be contiguous unless
+    `strided` (token-major views, checked by _operands)."""
     dev = ts[0].device
     for t in ts:
         if t.device.type != "cuda":
             raise ValueError("operands must be CUDA tensors")
         if t.device != dev:
             raise ValueError("operands must share one device")
-        if not t.is_contiguous():
+        if not strided and not t.is_contiguous():
             raise ValueError("operands must be contiguous")
     return dev
 
@@ -113,9 +115,11 @@ def _operands(tensors, layouts):
     ts = 0
     if len(strides) == 1 and None not in strides:
         ts = strides.pop()
-    out = [t if (lay == "token" and ts) or t.is_contiguous() else t.contiguous()
-           for t, lay in zip(tensors, layouts)]
-    return out, ts
+    for t, lay in zip(tensors, layouts):
+        if not t.is_contiguous() and not (lay == "token" and ts):
+            raise ValueError("operands must be contiguous, or token-major views with dense "
+                             "heads and one shared token stride")
+    return list(tensors), ts
 
 
 def prefill(q, k, v, *, scale: float = 1.0, q_layout="heads", k_layout="heads",
@@ -126,7 +130,7 @@ def prefill(q, k, v, *, scale: float = 1.0, q_layout="heads", k_layout="heads",
     Layouts: "heads" (B,H,N,64), "token" (B,N,H,64) and, for k only, "kt"
     (B,H,64,N).  Returns out (and lse (B,H,Nq) or (H,B*Nq) when with_lse).
     """
-    dev = _need_cuda(q, k, v)
+    dev = _need_cuda(q, k, v, strided=True)
     B, H, Nq = _dims(q, q_layout)
     _, _, cap = _dims(k, k_layout)
     Nk = cap if kv_len is None else kv_len
@@ -208,7 +212,7 @@ def varlen(q, k, v, cu_seqlens_q, cu_seqlens_k=None, *, scale: float = 1.0,
 
     Segment s attends only within itself.  Returns out (T,H,64) [, lse (H,T)].
     """
-    dev = _need_cuda(q, k, v)
+    dev = _need_cuda(q, k, v, strided=True)
     if q.dim() != 3 or q.shape[-1] != 64:
         raise ValueError("varlen operands are (T, H, 64)")
     T, H = q.shape[0], q.shape[1]
