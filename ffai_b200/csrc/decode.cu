@@ -324,21 +324,34 @@ __global__ void __launch_bounds__(kClThreads, 2) decode_cluster_kernel(DecodePar
   float* wslot = reinterpret_cast<float*>(empty + kClStages);  // [8][66] per-warp partials
   float* cslot = wslot + kClWarps * kClSlot;                   // [8][66] per-CTA partials (leader)
   __shared__ int s_abort;
+  __shared__ int s_page[32];  // paged: the first 32 stages' pages, loaded in parallel
 
   const int tid = threadIdx.x, warp = tid / 32, lane = tid % 32;
   const int rank = S > 1 ? static_cast<int>(cluster_ctarank()) : 0;
   const int row = blockIdx.x / S;
   if (S > 1) cluster_arrive_relaxed();  // paired with the wait before the merge
   griddep_launch_dependents();
-  int len = p.kv_len, kp = kpc;
+  int len = p.kv_len;
   if constexpr (PAGED) {
-    // The lengths (and tables) may come from the preceding kernel (an append).
+    // kpc is page-aligned and comes from the host's length bound, so this
+    // CTA's range start, and the pages of its first 32 stages, are known
+    // before the dependency wait; the block table is written by the host,
+    // not by the preceding kernel.  The lengths may come from the preceding
+    // kernel (an append), so they are read after the wait.
+    if (warp == kClWarps) {
+      const int slot = (rank * kpc + lane * KS) / kPageKeys;
+      if (lane * KS < kpc && slot < p.max_pages)
+        s_page[lane] = __ldcg(p.block_table + static_cast<size_t>(row / p.heads) * p.max_pages + slot);
+    }
     griddep_wait();
     len = min(max(__ldcg(p.seq_lens + row / p.heads), 0), p.max_pages * kPageKeys);
-    kp = ((len + S - 1) / S + kPageKeys - 1) / kPageKeys * kPageKeys;  // page-aligned ranges
+    if (len > S * kpc) {  // longer than the caller's bound: not covered, reported
+      if (tid == 0 && rank == S - 1 && p.err) atomicOr(p.err, kErrBadArgs);
+      len = S * kpc;
+    }
   }
-  const int k0 = min(len, rank * kp);
-  const int k1 = min(len, k0 + kp);
+  const int k0 = min(len, rank * kpc);
+  const int k1 = min(len, k0 + kpc);
   const int nch = (k1 - k0 + KS - 1) / KS;
 
   if (tid == 0) {
@@ -355,6 +368,7 @@ __global__ void __launch_bounds__(kClThreads, 2) decode_cluster_kernel(DecodePar
   if (warp == kClWarps) {
     // Producer: all of the range's stages at once, then refills as warps free them.
     if (!p.kv_stable) griddep_wait();
+    if constexpr (PAGED) __syncwarp();  // s_page written by the warp's lanes
     if (lane == 0) {
       int issued = 0;
       for (int c = 0; c < nch; ++c) {
@@ -370,9 +384,11 @@ __global__ void __launch_bounds__(kClThreads, 2) decode_cluster_kernel(DecodePar
           // A stage never crosses a page: ranges start on page boundaries and
           // KS divides kPageKeys.
           const int j0 = k0 + c * KS;
-          const int page = __ldcg(p.block_table +
-                                  static_cast<size_t>(row / p.heads) * p.max_pages +
-                                  j0 / kPageKeys);
+          const int page = (c < 32 && k0 == rank * kpc)
+                               ? s_page[c]
+                               : __ldcg(p.block_table +
+                                        static_cast<size_t>(row / p.heads) * p.max_pages +
+                                        j0 / kPageKeys);
           ok_src = page >= 0 && page < p.num_pages;
           off = ((static_cast<size_t>(page) * p.heads + row % p.heads) * kPageKeys +
                  j0 % kPageKeys) * 64;
@@ -597,13 +613,15 @@ cudaError_t launch_decode_cluster(const DecodeParams& p, int splits, int keys_pe
 
 cudaError_t launch_decode_paged(const DecodeParams& p, int splits, cudaStream_t s) {
   if (splits < 1 || splits > kDecodeMaxCluster) return cudaErrorInvalidValue;
+  // Page-aligned ranges over the length bound p.kv_len.
+  const int kpc = ((p.kv_len + splits - 1) / splits + kPageKeys - 1) / kPageKeys * kPageKeys;
   switch (p.kv_dtype) {
     case 0:
-      return launch_cluster_t<float, true>(p, splits, 0, s);
+      return launch_cluster_t<float, true>(p, splits, kpc, s);
     case 1:
-      return launch_cluster_t<__nv_bfloat16, true>(p, splits, 0, s);
+      return launch_cluster_t<__nv_bfloat16, true>(p, splits, kpc, s);
     case 2:
-      return launch_cluster_t<__half, true>(p, splits, 0, s);
+      return launch_cluster_t<__half, true>(p, splits, kpc, s);
   }
   return cudaErrorInvalidValue;
 }

@@ -188,9 +188,12 @@ int ffai_attn_decode_static(const ffai_attn_desc* d, const void* q, const void* 
 
 /* Decode over a paged cache: q (batch, heads, 1, 64) against each
  * sequence's seq_lens[b] keys (read on the device, so an append queued just
- * before on the stream is seen).  d->kv_len, when > 0, bounds the lengths for
- * the work split.  Rows with no keys give zeros.  Page ids outside
- * [0, num_pages) are not read; ffai_attn_sync then reports
+ * before on the stream is seen).  d->kv_len, when > 0, is an upper bound of
+ * the lengths that sets the work split (0: the table's reach, max_pages * 64);
+ * the block table must not be written by the kernel queued just before (the
+ * host writes it), since it is read ahead of that kernel's completion.  Rows
+ * with no keys give zeros.  Page ids outside [0, num_pages), or a length
+ * above the bound, are not read: ffai_attn_sync then reports
  * FFAI_ATTN_ERR_INVALID. */
 int ffai_attn_decode_paged(ffai_attn_ctx* ctx, const ffai_attn_desc* d, const void* q,
                            const void* k_pool, const void* v_pool, int32_t num_pages,

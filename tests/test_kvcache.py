@@ -151,3 +151,18 @@ def test_bad_page_id_is_reported_not_read():
     with pytest.raises(attention.AttnError) as e:
         attention.sync(0)
     assert e.value.status == -1  # FFAI_ATTN_ERR_INVALID
+
+
+@pytest.mark.gpu
+def test_length_above_the_bound_is_reported():
+    from ffai_b200 import attention
+    from ffai_b200.kvcache import decode_paged
+    B, H, num_pages = 2, 4, 8
+    kp = torch.zeros(num_pages, H, PAGE_KEYS, 64, dtype=torch.bfloat16, device=DEV)
+    table = torch.arange(8, dtype=torch.int32, device=DEV).view(2, 4)
+    lens = torch.tensor([200, 100], dtype=torch.int32, device=DEV)
+    q = torch.zeros(B, H, 1, 64, device=DEV)
+    decode_paged(q, kp, kp, table, lens, kv_bound=64)   # bound below beam 0's length
+    with pytest.raises(attention.AttnError) as e:
+        attention.sync(0)
+    assert e.value.status == -1
