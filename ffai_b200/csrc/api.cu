@@ -264,7 +264,8 @@ void init_encoder() {
 // 3-d bf16/f16 tensor map over 64-element (128-byte) rows with a box of 128
 // rows and 128-byte swizzle.  token_major: dims {64, H, T}; else {64, rows, B*H}.
 int make_map(ffai_attn_ctx* ctx, CUtensorMap* map, const void* base, bool token_major, int H,
-             long long rows_or_tokens, long long groups, long long token_stride = 0) {
+             long long rows_or_tokens, long long groups, long long token_stride = 0,
+             int box_rows = kTcRows) {
   if (!g_encode) return set_error(ctx, FFAI_ATTN_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
   if (reinterpret_cast<uintptr_t>(base) % 16 != 0)
     return set_error(ctx, FFAI_ATTN_ERR_INVALID, "operand base address not 16-byte aligned");
@@ -280,7 +281,7 @@ int make_map(ffai_attn_ctx* ctx, CUtensorMap* map, const void* base, bool token_
     strides[1] = static_cast<cuuint64_t>(token_stride > 0 ? token_stride : H * kHD) * 2;
     box[0] = kHD;
     box[1] = 1;
-    box[2] = kTcRows;
+    box[2] = static_cast<cuuint32_t>(box_rows);
   } else {
     dims[0] = kHD;
     dims[1] = static_cast<cuuint64_t>(rows_or_tokens);
@@ -288,7 +289,7 @@ int make_map(ffai_attn_ctx* ctx, CUtensorMap* map, const void* base, bool token_
     strides[0] = kHD * 2;
     strides[1] = static_cast<cuuint64_t>(rows_or_tokens) * kHD * 2;
     box[0] = kHD;
-    box[1] = kTcRows;
+    box[1] = static_cast<cuuint32_t>(box_rows);
     box[2] = 1;
   }
   // The data type only sets the element size here (both are 2 bytes).
@@ -409,6 +410,14 @@ int run_tc(ffai_attn_ctx* ctx, const Operand& q, const Operand& k, const Operand
   if (st) return st;
   st = make_map(ctx, &tv, v.ptr, v.token_major, H, v.rows, v.groups, v.token_stride);
   if (st) return st;
+  // bf16 output: a map of 16-row boxes for the kernel's TMA-store epilogue.
+  CUtensorMap to = tq;
+  const bool o_tma = out_bf16 && reinterpret_cast<uintptr_t>(o) % 16 == 0;
+  if (o_tma) {
+    st = out_tm ? make_map(ctx, &to, o, true, H, lse_tokens, 1, 0, 16)
+                : make_map(ctx, &to, o, false, H, out_rows, q.groups, 0, 16);
+    if (st) return st;
+  }
   TcParams p{};
   p.units = ctx->d_units;
   p.num_units = ctx->wl_units;
@@ -430,9 +439,10 @@ int run_tc(ffai_attn_ctx* ctx, const Operand& q, const Operand& k, const Operand
   p.err = ctx->d_err;
   p.causal = causal;
   p.q_offset = q_offset;
+  p.o_tma = o_tma ? 1 : 0;
   const int grid = std::min(ctx->wl_units, ctx->num_sms);
   if (grid <= 0) return FFAI_ATTN_OK;
-  FFAI_CUDA(ctx, launch_prefill_tc(tq, tk, tv, p, grid, ab_f16, s));
+  FFAI_CUDA(ctx, launch_prefill_tc(tq, tk, tv, to, p, grid, ab_f16, s));
   return FFAI_ATTN_OK;
 }
 

@@ -130,6 +130,7 @@ struct TcParams {
   unsigned* err;
   int causal;    // key j visible to query row i (within its sequence) iff j <= q_offset + i
   int q_offset;  // >= 0
+  int o_tma;     // 1: bf16 output through the tmO tensor map (16-row boxes)
 };
 
 // Key blocks (of kTcKeys) that tile t (0, 1) of a unit needs: all of the
@@ -149,8 +150,8 @@ __host__ __device__ inline int tc_tile_blocks(int causal, int q_offset, int q_le
 // tm*: 3-d tensor maps built by the host for 128-row x 64-col boxes with
 // 128-byte swizzle.  ab_f16: 1 for f16 operands, 0 for bf16.
 cudaError_t launch_prefill_tc(const CUtensorMap& tmQ, const CUtensorMap& tmK,
-                              const CUtensorMap& tmV, const TcParams& p, int grid, int ab_f16,
-                              cudaStream_t s);
+                              const CUtensorMap& tmV, const CUtensorMap& tmO, const TcParams& p,
+                              int grid, int ab_f16, cudaStream_t s);
 size_t prefill_tc_smem_bytes();
 
 // ---- conversions (convert.cu) -----------------------------------------------

@@ -63,7 +63,10 @@ struct __align__(8) TcBars {
 };
 
 // Q0, Q1, and the K and V rings, then the barriers.
-constexpr size_t kSmemTiles = (2 + 2 * kTcStages) * kTileBytes;
+// Output staging for the TMA-store epilogue: per softmax warp, 16 rows of
+// 64 bf16 (2 KB) in the 128-byte-swizzled layout of the output tensor map.
+constexpr uint32_t kStageBytes = 16 * 128;
+constexpr size_t kSmemTiles = (2 + 2 * kTcStages) * kTileBytes + 16 * kStageBytes;
 constexpr size_t kSmemBytes = kSmemTiles + sizeof(TcBars) + 1024;  // +1024: alignment slack
 
 __device__ __forceinline__ void unit_at(const TcParams& p, int u, TcUnit& out) {
@@ -417,7 +420,8 @@ __device__ __forceinline__ void exp_pack_rows(const float* sf, float sl2, const 
 // rows lb + t1 and lb + t1 + 8, a quarter of each row's columns; the four
 // threads of a row reduce its max and sum with two shuffles.
 template <int AB_F16, bool CAUSAL>
-__device__ __forceinline__ void run_softmax(const TcParams& p, uint32_t tmem, TcBars* bars) {
+__device__ __forceinline__ void run_softmax(const TcParams& p, uint32_t tmem, TcBars* bars,
+                                            const CUtensorMap* tmO, uint8_t* sO) {
   volatile int* abort_flag = &bars->abort_flag;
   const int warp = threadIdx.x / 32;
   const int lane = threadIdx.x % 32;
@@ -549,14 +553,51 @@ __device__ __forceinline__ void run_softmax(const TcParams& p, uint32_t tmem, Tc
     tmem_ld_16x256b_x8(tO, orr);
     tmem_wait_ld();
     const int q_len = __ldg(p.q_len + w.seq);
+    const int row_base = w.row0 + t * kTcRows + lb;  // the warp's 16 rows
+    // bf16 output with all 16 rows inside the sequence: one TMA store per
+    // warp from its staging buffer (the TMEM layout's 4-byte pieces are
+    // scattered over 8 rows; the tensor store writes whole rows).
+    const bool tma = p.o_tma && row_base + 16 <= q_len;
+    uint8_t* stg = sO + warp * kStageBytes;
+    if (tma) {
+      if (lane == 0) bulk_wait_read_all();  // the previous store has read the buffer
+      __syncwarp();
+    }
 #pragma unroll
     for (int v = 0; v < 2; ++v) {
       float l = l_run[v];
       l += __shfl_xor_sync(0xffffffffu, l, 1);
       l += __shfl_xor_sync(0xffffffffu, l, 2);
-      const int row = w.row0 + t * kTcRows + lb + t1 + 8 * v;
-      if (row < q_len) {
+      l_run[v] = l;
+      const int row = row_base + t1 + 8 * v;
+      if (tma) {
+        // row r = t1 + 8 v of the box, 16-byte chunk k at k ^ (r % 8) = k ^ t1
+        const float inv = 1.f / l;
+#pragma unroll
+        for (int k = 0; k < 8; ++k)
+          *reinterpret_cast<uint32_t*>(stg + (t1 + 8 * v) * 128 + ((k ^ t1) << 4) + 4 * t0) =
+              pack_bf16x2(__uint_as_float(orr[4 * k + 2 * v]) * inv,
+                          __uint_as_float(orr[4 * k + 2 * v + 1]) * inv);
+      } else if (row < q_len) {
         store_row_quarter(p, w, row, t0, orr, v, 1.f / l);
+      }
+    }
+    if (tma) {
+      fence_proxy_async_smem();  // the generic-proxy writes, seen by the tensor store
+      __syncwarp();
+      if (lane == 0) {
+        if (p.out_token_major)
+          tma_store_3d(tmO, stg, 0, w.head, __ldg(p.q_start + w.seq) + row_base);
+        else
+          tma_store_3d(tmO, stg, 0, row_base, w.seq * p.heads + w.head);
+        bulk_commit();
+      }
+    }
+#pragma unroll
+    for (int v = 0; v < 2; ++v) {
+      const float l = l_run[v];
+      const int row = row_base + t1 + 8 * v;
+      if (row < q_len) {
         if (p.lse && t0 == 0) {
           const float lse = (m_run[v] + __log2f(l)) * 0.69314718055994530942f;
           if (p.out_token_major)
@@ -576,14 +617,16 @@ template <int AB_F16, bool CAUSAL>
 __global__ void __launch_bounds__(kTcThreads, 1)
     prefill_tc_kernel(const __grid_constant__ CUtensorMap tmQ,
                       const __grid_constant__ CUtensorMap tmK,
-                      const __grid_constant__ CUtensorMap tmV, const TcParams p) {
+                      const __grid_constant__ CUtensorMap tmV,
+                      const __grid_constant__ CUtensorMap tmO, const TcParams p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~static_cast<uintptr_t>(1023));
   uint8_t* sQ = smem;
   uint8_t* sK = sQ + 2 * kTileBytes;
   uint8_t* sV = sK + kTcStages * kTileBytes;
-  TcBars* bars = reinterpret_cast<TcBars*>(sV + kTcStages * kTileBytes);
+  uint8_t* sO = sV + kTcStages * kTileBytes;  // 16 x kStageBytes, 1024-byte aligned
+  TcBars* bars = reinterpret_cast<TcBars*>(sO + 16 * kStageBytes);
 
   const int warp = threadIdx.x / 32;
   const int lane = threadIdx.x % 32;
@@ -614,6 +657,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     prefetch_tensormap(&tmQ);
     prefetch_tensormap(&tmK);
     prefetch_tensormap(&tmV);
+    if (p.o_tma) prefetch_tensormap(&tmO);
   }
   tc_fence_before();
   __syncthreads();
@@ -631,7 +675,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       mbar_wait(&bars->drain, 0, &none, p.err, kErrTimeoutDrain);
     }
   } else {
-    run_softmax<AB_F16, CAUSAL>(p, tmem, bars);
+    run_softmax<AB_F16, CAUSAL>(p, tmem, bars, &tmO, sO);
+    if (lane == 0 && p.o_tma) bulk_wait_all();  // output stores complete before exit
   }
 
   __syncwarp();
@@ -648,15 +693,16 @@ __global__ void __launch_bounds__(kTcThreads, 1)
 size_t prefill_tc_smem_bytes() { return kSmemBytes; }
 
 cudaError_t launch_prefill_tc(const CUtensorMap& tmQ, const CUtensorMap& tmK,
-                              const CUtensorMap& tmV, const TcParams& p, int grid, int ab_f16,
-                              cudaStream_t s) {
+                              const CUtensorMap& tmV, const CUtensorMap& tmO, const TcParams& p,
+                              int grid, int ab_f16, cudaStream_t s) {
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return e;
   static bool configured[4][64] = {};
   if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
   const int which = ab_f16 * 2 + (p.causal ? 1 : 0);
-  void (*kern)(const CUtensorMap, const CUtensorMap, const CUtensorMap, const TcParams) =
+  void (*kern)(const CUtensorMap, const CUtensorMap, const CUtensorMap, const CUtensorMap,
+               const TcParams) =
       which == 0   ? prefill_tc_kernel<0, false>
       : which == 1 ? prefill_tc_kernel<0, true>
       : which == 2 ? prefill_tc_kernel<1, false>
@@ -667,7 +713,7 @@ cudaError_t launch_prefill_tc(const CUtensorMap& tmQ, const CUtensorMap& tmK,
     if (e != cudaSuccess) return e;
     configured[which][dev] = true;
   }
-  kern<<<grid, kTcThreads, kSmemBytes, s>>>(tmQ, tmK, tmV, p);
+  kern<<<grid, kTcThreads, kSmemBytes, s>>>(tmQ, tmK, tmV, tmO, p);
   return cudaGetLastError();
 }
 

@@ -296,3 +296,34 @@ def test_fused_qkv_views_varlen():
     ref = attention.varlen(qkv[:, 0].contiguous(), qkv[:, 1].contiguous(),
                            qkv[:, 2].contiguous(), cu, scale=S)
     assert torch.equal(got, ref)
+
+
+@pytest.mark.parametrize("N", [1, 15, 16, 17, 127, 129, 300, 1500])
+@pytest.mark.parametrize("layout", ["heads", "token"])
+def test_bf16_output_equals_rounded_f32_output(N, layout):
+    """bf16 output (whole 16-row groups go out through the tensor-store
+    epilogue, ragged ones through plain stores) is exactly the f32 output
+    rounded to bf16, at lengths around the 16-row groups and tiles."""
+    q, k, v = _inputs(2, 3, N, seed=60 + N)
+    qd, kd, vd = q.to(DEV), k.to(DEV), v.to(DEV)
+    kw = dict(scale=S, out_layout=layout)
+    if layout == "token":
+        qd, kd, vd = (x.transpose(1, 2).contiguous() for x in (qd, kd, vd))
+        kw.update(q_layout="token", k_layout="token", v_layout="token")
+    f32 = attention.prefill(qd, kd, vd, out_dtype=torch.float32, **kw)
+    b16 = attention.prefill(qd, kd, vd, out_dtype=torch.bfloat16, **kw)
+    assert torch.equal(b16, f32.to(torch.bfloat16))
+
+
+def test_bf16_output_varlen_equals_rounded_f32():
+    g = torch.Generator().manual_seed(61)
+    lens = [200, 16, 333, 129, 1]
+    T, H = sum(lens), 4
+    q, k, v = ((torch.randn(T, H, 64, generator=g) * 0.5).to(torch.bfloat16).to(DEV)
+               for _ in range(3))
+    cu = [0]
+    for L in lens:
+        cu.append(cu[-1] + L)
+    f32 = attention.varlen(q, k, v, cu, scale=S, out_dtype=torch.float32)
+    b16 = attention.varlen(q, k, v, cu, scale=S, out_dtype=torch.bfloat16)
+    assert torch.equal(b16, f32.to(torch.bfloat16))
