@@ -14,6 +14,8 @@
 // the chunk's P.V, and writes a partial (m, l, o[64]) to the workspace.  The
 // last CTA of a row to finish (an atomic ticket) combines the partials, so a
 // decode step is a single launch.
+#include <atomic>
+
 #include "common.cuh"
 #include "kernels.h"
 
@@ -568,13 +570,13 @@ cudaError_t launch_cluster_t(const DecodeParams& p, int S, int kpc, cudaStream_t
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return e;
-  static bool configured[64] = {};
+  static std::atomic<bool> configured[64];  // per device; racing first calls both set it
   if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
-  if (!configured[dev]) {
+  if (!configured[dev].load(std::memory_order_acquire)) {
     e = cudaFuncSetAttribute(decode_cluster_kernel<T, PAGED>,
                              cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
     if (e != cudaSuccess) return e;
-    configured[dev] = true;
+    configured[dev].store(true, std::memory_order_release);
   }
   cudaLaunchConfig_t cfg{};
   cfg.gridDim = dim3(static_cast<unsigned>(p.rows) * S);

@@ -10,6 +10,8 @@
 // scores, keys tx+16c (c < 4); for the output, head dims tx+16c.  Each thread
 // also keeps the row sums of its four rows, accumulated in the P.V loop.  Shared
 // tiles are padded to 65 floats per row so every access is bank-conflict free.
+#include <atomic>
+
 #include "common.cuh"
 #include "kernels.h"
 
@@ -163,13 +165,13 @@ cudaError_t launch_prefill_simt(const SimtParams& p, cudaStream_t s) {
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return e;
-  static bool configured[64] = {};  // the attribute is per device
+  static std::atomic<bool> configured[64];  // the attribute is per device
   if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
-  if (!configured[dev]) {
+  if (!configured[dev].load(std::memory_order_acquire)) {
     e = cudaFuncSetAttribute(prefill_simt_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              static_cast<int>(smem));
     if (e != cudaSuccess) return e;
-    configured[dev] = true;
+    configured[dev].store(true, std::memory_order_release);
   }
   dim3 grid((p.Nq + kBM - 1) / kBM, p.B * p.H);
   prefill_simt_kernel<<<grid, 256, smem, s>>>(p);

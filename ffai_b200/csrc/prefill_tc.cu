@@ -39,6 +39,8 @@
 //
 // Every wait is bounded (common.cuh); on a timeout the CTA raises an error
 // bit, drains its MMAs and TMA loads, frees TMEM and exits.
+#include <atomic>
+
 #include "common.cuh"
 #include "kernels.h"
 
@@ -698,7 +700,7 @@ cudaError_t launch_prefill_tc(const CUtensorMap& tmQ, const CUtensorMap& tmK,
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return e;
-  static bool configured[4][64] = {};
+  static std::atomic<bool> configured[4][64];  // racing first calls both set it
   if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
   const int which = ab_f16 * 2 + (p.causal ? 1 : 0);
   void (*kern)(const CUtensorMap, const CUtensorMap, const CUtensorMap, const CUtensorMap,
@@ -707,11 +709,11 @@ cudaError_t launch_prefill_tc(const CUtensorMap& tmQ, const CUtensorMap& tmK,
       : which == 1 ? prefill_tc_kernel<0, true>
       : which == 2 ? prefill_tc_kernel<1, false>
                    : prefill_tc_kernel<1, true>;
-  if (!configured[which][dev]) {
+  if (!configured[which][dev].load(std::memory_order_acquire)) {
     e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              static_cast<int>(kSmemBytes));
     if (e != cudaSuccess) return e;
-    configured[which][dev] = true;
+    configured[which][dev].store(true, std::memory_order_release);
   }
   kern<<<grid, kTcThreads, kSmemBytes, s>>>(tmQ, tmK, tmV, tmO, p);
   return cudaGetLastError();
