@@ -335,6 +335,88 @@ def bench_decode_paged(steps: int, dev):
             "us_per_launch_graph": round(t * 1e6, 2), "gbs_graph": round(bytes_per / t / 1e9, 1)}
 
 
+def bench_int8_gemv(steps: int, dev):
+    """The decoder's block-scaled int8 GEMV (the reference's Int8Vocab, blk
+    32): the vocabulary projection (51865 x 1280, large-v3) for 1 and 5
+    activation rows, and the MLP's fc1/fc2 (5120 x 1280, 1280 x 5120) over 32
+    layers; weights rotate over copies larger than L2.  Beside it, the
+    oracle's restatement of the reference's CPU GEMV on the host cores."""
+    import numpy as np
+    import torch
+
+    from ffai_b200.int8_gemv import Int8Gemv
+    from oracle import oracle
+    res = {}
+    g = torch.Generator(device=dev).manual_seed(9)
+
+    def algo_bytes(q, batch):
+        nb = q.cols // q.blk
+        return q.rows * (q.cols + 4 * nb + 4) + batch * 4 * (q.cols + q.rows)
+
+    def time_calls(calls, reps):
+        for _ in range(3):
+            for c in calls:
+                c()
+        torch.cuda.synchronize()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        for _ in range(reps):
+            for c in calls:
+                c()
+        b.record()
+        torch.cuda.synchronize()
+        return a.elapsed_time(b) / 1e3 / (reps * len(calls))
+
+    vocab = [Int8Gemv.new(torch.randn(51865, 1280, device=dev, generator=g) * 0.05)
+             for _ in range(3)]
+    for batch in (1, 5):
+        x = torch.randn(batch, 1280, device=dev, generator=g)
+        outs = [torch.empty(batch, 51865, device=dev) for _ in vocab]
+        t = time_calls([lambda q=q, o=o: q.forward(x, out=o) for q, o in zip(vocab, outs)],
+                       max(4, steps))
+        nbytes = algo_bytes(vocab[0], batch)
+        res[f"vocab_51865x1280_b{batch}"] = {
+            "kernel": "int8_gemv_kernel", "bytes_per_launch": nbytes,
+            "us_per_launch": round(t * 1e6, 2), "gbs": round(nbytes / t / 1e9, 1)}
+    del vocab
+    layers = 32
+    fc1 = [Int8Gemv.new(torch.randn(5120, 1280, device=dev, generator=g) * 0.05)
+           for _ in range(layers)]
+    fc2 = [Int8Gemv.new(torch.randn(1280, 5120, device=dev, generator=g) * 0.05)
+           for _ in range(layers)]
+    x1 = torch.randn(5, 1280, device=dev, generator=g)
+    x2 = torch.randn(5, 5120, device=dev, generator=g)
+    o1, o2 = torch.empty(5, 5120, device=dev), torch.empty(5, 1280, device=dev)
+    calls = []
+    for a1, a2 in zip(fc1, fc2):
+        calls += [lambda q=a1: q.forward(x1, out=o1), lambda q=a2: q.forward(x2, out=o2)]
+    t = time_calls(calls, max(2, steps // 2))
+    nbytes = (algo_bytes(fc1[0], 5) + algo_bytes(fc2[0], 5)) / 2
+    res["mlp_fc1_fc2_b5"] = {"kernel": "int8_gemv_kernel", "layers": layers,
+                             "bytes_per_launch": int(nbytes), "us_per_launch": round(t * 1e6, 2),
+                             "gbs": round(nbytes / t / 1e9, 1)}
+    del fc1, fc2
+    # the reference's CPU GEMV (oracle restatement, all host threads), 1 row
+    oracle.build()
+    rng = np.random.default_rng(3)
+    w = rng.standard_normal((51865, 1280), dtype=np.float32) * np.float32(0.05)
+    qw, bs, corr = oracle.int8_quantize(w, 32)
+    xn = rng.standard_normal((1, 1280), dtype=np.float32)
+    threads = os.cpu_count() or 1
+    oracle.int8_gemv(xn, qw, bs, corr, 32, threads=threads)
+    runs, t0 = 0, time.perf_counter()
+    while time.perf_counter() - t0 < 2.0 or runs == 0:
+        oracle.int8_gemv(xn, qw, bs, corr, 32, threads=threads)
+        runs += 1
+    tc = (time.perf_counter() - t0) / runs
+    nbytes = 51865 * (1280 + 4 * 40 + 4) + 4 * (1280 + 51865)
+    res["cpu_vocab_51865x1280_b1"] = {
+        "kind": "port", "cores": threads, "us_per_call": round(tc * 1e6, 1),
+        "gbs": round(nbytes / tc / 1e9, 2),
+        "sample": f"{runs} call(s) of the oracle's vocab_int8.rs restatement, 1 activation row"}
+    return res
+
+
 def bench_ragged(dist, steps: int, peaks):
     """c5: 256 packed segments of U{200..1500} frames, 16 heads, through the
     varlen entry; segments assigned to ranks longest-processing-time first on
@@ -515,6 +597,13 @@ def run_ours(args, dist):
         for v_ in decode.values():
             v_["frac_of_hbm"] = round(v_["gbs_graph"] / peaks["hbm_gbs"], 4)
 
+    int8 = None
+    if dist.rank == 0 and not args.no_int8:
+        int8 = bench_int8_gemv(max(5, min(args.steps, 50)), torch.device("cuda", torch.cuda.current_device()))
+        for k_, v_ in int8.items():
+            if not k_.startswith("cpu"):
+                v_["frac_of_hbm"] = round(v_["gbs"] / peaks["hbm_gbs"], 4)
+
     cpu = None
     if dist.rank == 0 and dist.world == 1 and not args.no_cpu_baseline:
         rate, threads, sample, _, data = cpu_encoder_rate(cfg, budget_s=args.cpu_seconds)
@@ -552,6 +641,7 @@ def run_ours(args, dist):
             "clocks": clocks.summary(),
             "decode": decode,
             "ragged_c5": ragged,
+            "int8_gemv": int8,
         }
         print(json.dumps(line), flush=True)
     dist.barrier()
@@ -567,6 +657,7 @@ def main():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-decode", action="store_true")
     ap.add_argument("--no-ragged", action="store_true")
+    ap.add_argument("--no-int8", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--segments", type=int, default=0,

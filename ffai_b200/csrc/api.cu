@@ -1366,3 +1366,78 @@ extern "C" int ffai_attn_decode_static(const ffai_attn_desc* d, const void* q, c
   if (e != cudaSuccess) return cuda_fail(nullptr, e, "launch_decode");
   return FFAI_ATTN_OK;
 }
+
+// ---------------------------------------------------------------------------
+// int8 GEMV (the reference's Int8Vocab, vocab_int8.rs)
+
+extern "C" {
+
+int ffai_int8_gemv_layout(int32_t rows, int32_t cols, int32_t blk, int64_t* qw_bytes,
+                          int64_t* scale_count, int64_t* corr_count) {
+  if (rows <= 0 || !int8_gemv_served(cols, blk))
+    return set_error(nullptr, FFAI_ATTN_DECLINED,
+                     "int8 GEMV: blk %d must be a multiple of 32 up to %d dividing cols %d "
+                     "(at most %d)", blk, kGvMaxBlk, cols, kGvMaxCols);
+  const long long padded = int8_gemv_groups(rows) * 32;
+  if (qw_bytes) *qw_bytes = padded * cols;
+  if (scale_count) *scale_count = padded * (cols / blk);
+  if (corr_count) *corr_count = padded;
+  return FFAI_ATTN_OK;
+}
+
+int ffai_int8_gemv_quantize(ffai_attn_ctx* ctx, const void* w, int32_t w_dtype, int32_t rows,
+                            int32_t cols, int32_t blk, int8_t* qw, float* bscale, float* corr,
+                            void* stream) {
+  if (!ctx) return set_error(nullptr, FFAI_ATTN_ERR_INVALID, "null context");
+  if (rows <= 0 || !int8_gemv_served(cols, blk))
+    return set_error(ctx, FFAI_ATTN_DECLINED,
+                     "int8 GEMV: blk %d must be a multiple of 32 up to %d dividing cols %d "
+                     "(at most %d)", blk, kGvMaxBlk, cols, kGvMaxCols);
+  if (!valid_dtype(w_dtype)) return set_error(ctx, FFAI_ATTN_ERR_INVALID, "unknown weight dtype");
+  if (!w || !qw || !bscale || !corr)
+    return set_error(ctx, FFAI_ATTN_ERR_INVALID, "int8 GEMV quantize: null pointer");
+  DeviceGuard g(ctx->device);
+  FFAI_CUDA(ctx, launch_int8_quantize(w, w_dtype, rows, cols, blk, qw, bscale, corr,
+                                      static_cast<cudaStream_t>(stream)));
+  return FFAI_ATTN_OK;
+}
+
+int ffai_int8_gemv(ffai_attn_ctx* ctx, const float* x, int32_t batch, const int8_t* qw,
+                   const float* bscale, const float* corr, int32_t rows, int32_t cols,
+                   int32_t blk, float* out, uint32_t flags, void* stream) {
+  if (!ctx) return set_error(nullptr, FFAI_ATTN_ERR_INVALID, "null context");
+  if (flags & ~FFAI_INT8_FLAG_WEIGHTS_STABLE)
+    return set_error(ctx, FFAI_ATTN_ERR_INVALID, "int8 GEMV: unknown flags 0x%x", flags);
+  if (rows <= 0 || !int8_gemv_served(cols, blk))
+    return set_error(ctx, FFAI_ATTN_DECLINED,
+                     "int8 GEMV: blk %d must be a multiple of 32 up to %d dividing cols %d "
+                     "(at most %d)", blk, kGvMaxBlk, cols, kGvMaxCols);
+  if (batch < 1 || batch > kGvMaxBatch)
+    return set_error(ctx, FFAI_ATTN_ERR_INVALID, "int8 GEMV: batch %d not in [1, %d]", batch,
+                     kGvMaxBatch);
+  if (!x || !qw || !bscale || !corr || !out)
+    return set_error(ctx, FFAI_ATTN_ERR_INVALID, "int8 GEMV: null pointer");
+  for (const void* ptr : {static_cast<const void*>(qw), static_cast<const void*>(bscale)})
+    if (reinterpret_cast<uintptr_t>(ptr) % 16 != 0)
+      return set_error(ctx, FFAI_ATTN_ERR_INVALID, "int8 GEMV: weights and scales 16-byte aligned");
+  Int8GemvParams p{};
+  if (!int8_gemv_plan(rows, cols, blk, batch, ctx->num_sms, &p.plan))
+    return set_error(ctx, FFAI_ATTN_DECLINED, "int8 GEMV: no shared-memory plan for %d x %d",
+                     rows, cols);
+  DeviceGuard g(ctx->device);
+  p.x = x;
+  p.batch = batch;
+  p.qw = qw;
+  p.bscale = bscale;
+  p.corr = corr;
+  p.rows = rows;
+  p.cols = cols;
+  p.blk = blk;
+  p.out = out;
+  p.err = ctx->d_err;
+  p.weights_stable = (flags & FFAI_INT8_FLAG_WEIGHTS_STABLE) != 0;
+  FFAI_CUDA(ctx, launch_int8_gemv(p, static_cast<cudaStream_t>(stream)));
+  return FFAI_ATTN_OK;
+}
+
+}  // extern "C"

@@ -74,6 +74,54 @@ cudaError_t launch_kv_append(const DecodeParams& p, int batch, const void* k_new
 cudaError_t launch_kv_copy_pages(const DecodeParams& p, const int* src, const int* dst, int n,
                                  cudaStream_t s);
 
+// ---- int8 GEMV (gemv_int8.cu) ----------------------------------------------
+
+// Device layout of the quantised weights, G = ceil(rows / 32) groups of 32
+// rows (rows past `rows` are zero):
+//   qw     (G, cols / 16, 32, 16) int8: bytes [16c, 16c + 16) of row 32g + l
+//          at ((g * cols / 16 + c) * 32 + l) * 16, so lane l of a warp reads
+//          row 32g + l with conflict-free 16-byte loads;
+//   bscale (G, cols / blk, 32) f32: scale of block b of row 32g + l;
+//   corr   (G * 32) f32.
+constexpr int kGvMaxBatch = 8;
+constexpr int kGvMaxCols = 8192;
+constexpr int kGvMaxBlk = 1024;
+
+inline bool int8_gemv_served(int cols, int blk) {
+  return blk > 0 && blk % 32 == 0 && blk <= kGvMaxBlk && cols > 0 && cols % blk == 0 &&
+         cols <= kGvMaxCols;
+}
+__host__ __device__ inline long long int8_gemv_groups(long long rows) { return (rows + 31) / 32; }
+
+// Launch geometry, computed on the host.  CTA c takes the contiguous groups
+// [c * groups / grid, (c + 1) * groups / grid) in rounds of up to `nmax`
+// groups; `wpg` consumer warps share a group (each a subset of its blocks);
+// a round streams its groups' columns through the shared-memory ring in steps
+// of `S` blocks per group.
+struct Int8GemvPlan {
+  int groups, grid, nmax, wpg, S, stages;
+  int slot_bytes;   // one ring slot: nmax * S * (blk * 32 + 128)
+  int x_off, p_off, bar_off, smem;
+};
+bool int8_gemv_plan(int rows, int cols, int blk, int batch, int sms, Int8GemvPlan* plan);
+
+struct Int8GemvParams {
+  const float* x;       // (batch, cols) f32 activations
+  int batch;            // 1..8
+  const int8_t* qw;     // packed weights (layout above)
+  const float* bscale;  // packed block scales
+  const float* corr;    // (G * 32) activation-offset corrections
+  int rows, cols, blk;  // int8_gemv_served(cols, blk)
+  float* out;           // (batch, rows)
+  unsigned* err;
+  int weights_stable;   // weights not written by the preceding kernel
+  Int8GemvPlan plan;
+};
+
+cudaError_t launch_int8_quantize(const void* w, int w_dtype, int rows, int cols, int blk,
+                                 int8_t* qw, float* bscale, float* corr, cudaStream_t s);
+cudaError_t launch_int8_gemv(const Int8GemvParams& p, cudaStream_t s);
+
 // ---- checked f32 prefill (prefill_simt.cu) ---------------------------------
 
 // Element offset of (b, h, row, d) is b*sb + h*sh + row*sr + d*sd.

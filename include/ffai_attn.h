@@ -214,6 +214,47 @@ int ffai_kv_copy_pages(ffai_attn_ctx* ctx, const ffai_attn_desc* d, void* k_pool
                        int32_t num_pages, const int32_t* src_pages, const int32_t* dst_pages,
                        int32_t n, void* stream);
 
+/* ---- int8 GEMV ---------------------------------------------------------
+ * The reference's block-scaled int8 GEMV (Int8Vocab, vocab_int8.rs), which
+ * it runs for the vocabulary projection (text_decoder.rs:945-969) and the
+ * decoder MLP's single-row layers (:94-104, :210-226).  Same quantisation and
+ * arithmetic, so outputs equal the reference's bit for bit.  Weights W are
+ * (rows, cols) row-major; blk (the reference's FFAI_VOCAB_BLK, default 32) is
+ * a multiple of 32, at most 1024, dividing cols (at most 8192) -- other
+ * shapes are FFAI_ATTN_DECLINED, as Int8Vocab::new (:102-131) returns None.
+ *
+ * The quantised weights are kept in a device layout of their own, rows padded
+ * to G = ceil(rows / 32) groups of 32 (padding zero):
+ *   qw     int8 (G, cols / 16, 32, 16): bytes [16c, 16c + 16) of row 32g + l
+ *          at ((g * (cols / 16) + c) * 32 + l) * 16;
+ *   bscale f32  (G, cols / blk, 32): scale of block b of row 32g + l at
+ *          (g * (cols / blk) + b) * 32 + l;
+ *   corr   f32  (G * 32).
+ * Device buffers throughout. */
+
+/* Sizes of the three buffers for a (rows, cols) matrix: qw bytes, bscale and
+ * corr element counts.  FFAI_ATTN_DECLINED for shapes not served. */
+int ffai_int8_gemv_layout(int32_t rows, int32_t cols, int32_t blk, int64_t* qw_bytes,
+                          int64_t* scale_count, int64_t* corr_count);
+
+/* Int8Vocab::new (vocab_int8.rs:97-166) on the device: W of w_dtype (f32,
+ * bf16 or f16; widened to f32 exactly) into the layout above. */
+int ffai_int8_gemv_quantize(ffai_attn_ctx* ctx, const void* w, int32_t w_dtype, int32_t rows,
+                            int32_t cols, int32_t blk, int8_t* qw, float* bscale, float* corr,
+                            void* stream);
+
+/* Int8VocabOp::cpu_fwd (vocab_int8.rs:218-305) for `batch` (1..8) activation
+ * rows at once: x (batch, cols) f32 -> out (batch, rows) f32, each row
+ * quantised on its own as the reference does per call; the weights are read
+ * once for all rows.  qw and bscale 16-byte aligned.  flags: 0 or
+ * FFAI_INT8_FLAG_WEIGHTS_STABLE -- the weights were not written by the kernel
+ * launched just before on the stream, so the GEMV may start streaming them
+ * before that kernel ends (x is always read after it). */
+#define FFAI_INT8_FLAG_WEIGHTS_STABLE 0x2u
+int ffai_int8_gemv(ffai_attn_ctx* ctx, const float* x, int32_t batch, const int8_t* qw,
+                   const float* bscale, const float* corr, int32_t rows, int32_t cols,
+                   int32_t blk, float* out, uint32_t flags, void* stream);
+
 /* Variable-length (ragged) prefill over packed segments, TOKEN_MAJOR
  * (T, H, 64) operands and output.  Segment s owns query rows
  * [cu_seqlens_q[s], cu_seqlens_q[s+1]) and keys [cu_seqlens_k[s],

@@ -61,6 +61,8 @@ def lib():
             "ora_attend_merged": ([_f32p, _f32p, _f32p, _f32p, i, i, i, i, i], i),
             "ora_serves": ([i] * 8, i),
             "ora_three_op": ([_f32p, _f32p, _f32p, _f32p, i, i, i], None),
+            "ora_int8_quantize": ([_f32p, i, i, i, ctypes.c_void_p, _f32p, _f32p], i),
+            "ora_int8_gemv": ([_f32p, i, ctypes.c_void_p, _f32p, _f32p, i, i, i, _f32p, i], None),
         }
         for name, (args, res) in sig.items():
             fn = getattr(L, name)
@@ -255,3 +257,35 @@ def three_op(q, kt, v) -> np.ndarray:
     out = np.empty((1, h, qlen, HD), np.float32)
     lib().ora_three_op(_p(q), _p(kt), _p(v), _p(out), h, qlen, keys)
     return out
+
+
+# --------------------------------------------------------------------------
+# int8 GEMV (vocab_int8.rs), restated in vocab_int8_ref.cpp
+# --------------------------------------------------------------------------
+
+def int8_quantize(w, blk=32):
+    """Int8Vocab::new: w (vocab, d) -> (qw int8, bscale f32, corr f32), or
+    None when the shape is not served (blk or d not multiples as required)."""
+    w = _f32(w)
+    vocab, d = w.shape
+    qw = np.empty((vocab, d), np.int8)
+    nb = d // blk if blk > 0 and d % blk == 0 else 1
+    bscale = np.empty((vocab, nb), np.float32)
+    corr = np.empty(vocab, np.float32)
+    st = lib().ora_int8_quantize(_p(w), vocab, d, blk, qw.ctypes.data_as(ctypes.c_void_p),
+                                 _p(bscale), _p(corr))
+    if st != 0:
+        return None
+    return qw, bscale, corr
+
+
+def int8_gemv(x, qw, bscale, corr, blk=32, threads=None):
+    """Int8VocabOp::cpu_fwd per activation row: x (batch, d) -> (batch, vocab)."""
+    x = _f32(np.atleast_2d(x))
+    vocab, d = qw.shape
+    qw = np.ascontiguousarray(qw, np.int8)
+    out = np.empty((x.shape[0], vocab), np.float32)
+    lib().ora_int8_gemv(_p(x), x.shape[0], qw.ctypes.data_as(ctypes.c_void_p), _p(_f32(bscale)),
+                        _p(_f32(corr)), vocab, d, blk, _p(out), threads or default_threads())
+    return out
+
