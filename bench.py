@@ -354,17 +354,32 @@ def bench_int8_gemv(steps: int, dev):
         return q.rows * (q.cols + 4 * nb + 4) + batch * 4 * (q.cols + q.rows)
 
     def time_calls(calls, reps):
-        for _ in range(3):
+        """Seconds per call, the calls captured in one CUDA graph (a Python
+        call costs more than a launch of these kernels)."""
+        for c in calls:
+            c()
+        torch.cuda.synchronize()
+        gr = torch.cuda.CUDAGraph()
+        s = torch.cuda.Stream()
+        s.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(s):
             for c in calls:
                 c()
+            torch.cuda.synchronize()
+            with torch.cuda.graph(gr, stream=s):
+                for c in calls:
+                    c()
+        torch.cuda.current_stream().wait_stream(s)
+        for _ in range(3):
+            gr.replay()
         torch.cuda.synchronize()
         a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         a.record()
         for _ in range(reps):
-            for c in calls:
-                c()
+            gr.replay()
         b.record()
         torch.cuda.synchronize()
+        del gr
         return a.elapsed_time(b) / 1e3 / (reps * len(calls))
 
     vocab = [Int8Gemv.new(torch.randn(51865, 1280, device=dev, generator=g) * 0.05)

@@ -88,10 +88,9 @@ SIGNATURES = {
                                ctypes.c_int),
     "ffai_kv_append": ([_vp, _DescP, _vp, _vp, _i32, _vp, _vp, _i32, _vp, _vp, _vp], ctypes.c_int),
     "ffai_kv_copy_pages": ([_vp, _DescP, _vp, _vp, _i32, _vp, _vp, _i32, _vp], ctypes.c_int),
-    "ffai_int8_gemv_layout": ([_i32, _i32, _i32, _vp, _vp, _vp], ctypes.c_int),
-    "ffai_int8_gemv_quantize": ([_vp, _vp, _i32, _i32, _i32, _i32, _vp, _vp, _vp, _vp],
-                                ctypes.c_int),
-    "ffai_int8_gemv": ([_vp, _vp, _i32, _vp, _vp, _vp, _i32, _i32, _i32, _vp, ctypes.c_uint32, _vp],
+    "ffai_int8_gemv_layout": ([_i32, _i32, _i32, _vp, _vp], ctypes.c_int),
+    "ffai_int8_gemv_quantize": ([_vp, _vp, _i32, _i32, _i32, _i32, _vp, _vp, _vp], ctypes.c_int),
+    "ffai_int8_gemv": ([_vp, _vp, _i32, _vp, _vp, _i32, _i32, _i32, _vp, ctypes.c_uint32, _vp],
                        ctypes.c_int),
     "ffai_attn_profile": ([_vp, _i32, ctypes.POINTER(ctypes.c_double),
                            ctypes.POINTER(ctypes.c_int64)], ctypes.c_int),

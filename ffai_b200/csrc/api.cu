@@ -83,6 +83,9 @@ struct ffai_attn_ctx {
   cudaEvent_t ev_h2d[2] = {}, ev_comp[2] = {}, ev_d2h[2] = {};
   void* d_pipe = nullptr;
   size_t pipe_cap = 0;
+  // int8 GEMV: quantised activations and their scales, between its two kernels
+  uint8_t* d_gemv_x = nullptr;
+  size_t gemv_x_cap = 0;
   ffai_attn_ctx* pipe_ctx = nullptr;  // inner context used for the pipeline's kernels
   std::string last_error;
   int last_status = FFAI_ATTN_OK;
@@ -702,6 +705,7 @@ void ffai_attn_destroy(ffai_attn_ctx* ctx) {
   cudaFree(ctx->d_seq);
   cudaFree(ctx->d_stage);
   cudaFree(ctx->d_pipe);
+  cudaFree(ctx->d_gemv_x);
   for (int i = 0; i < 2; ++i) {
     if (ctx->ev_h2d[i]) cudaEventDestroy(ctx->ev_h2d[i]);
     if (ctx->ev_comp[i]) cudaEventDestroy(ctx->ev_comp[i]);
@@ -1372,39 +1376,37 @@ extern "C" int ffai_attn_decode_static(const ffai_attn_desc* d, const void* q, c
 
 extern "C" {
 
-int ffai_int8_gemv_layout(int32_t rows, int32_t cols, int32_t blk, int64_t* qw_bytes,
-                          int64_t* scale_count, int64_t* corr_count) {
+int ffai_int8_gemv_layout(int32_t rows, int32_t cols, int32_t blk, int64_t* packed_bytes,
+                          int64_t* corr_count) {
   if (rows <= 0 || !int8_gemv_served(cols, blk))
     return set_error(nullptr, FFAI_ATTN_DECLINED,
                      "int8 GEMV: blk %d must be a multiple of 32 up to %d dividing cols %d "
                      "(at most %d)", blk, kGvMaxBlk, cols, kGvMaxCols);
-  const long long padded = int8_gemv_groups(rows) * 32;
-  if (qw_bytes) *qw_bytes = padded * cols;
-  if (scale_count) *scale_count = padded * (cols / blk);
-  if (corr_count) *corr_count = padded;
+  const long long groups = int8_gemv_groups(rows);
+  if (packed_bytes) *packed_bytes = groups * (cols / blk) * int8_gemv_record(blk);
+  if (corr_count) *corr_count = groups * 32;
   return FFAI_ATTN_OK;
 }
 
 int ffai_int8_gemv_quantize(ffai_attn_ctx* ctx, const void* w, int32_t w_dtype, int32_t rows,
-                            int32_t cols, int32_t blk, int8_t* qw, float* bscale, float* corr,
-                            void* stream) {
+                            int32_t cols, int32_t blk, void* packed, float* corr, void* stream) {
   if (!ctx) return set_error(nullptr, FFAI_ATTN_ERR_INVALID, "null context");
   if (rows <= 0 || !int8_gemv_served(cols, blk))
     return set_error(ctx, FFAI_ATTN_DECLINED,
                      "int8 GEMV: blk %d must be a multiple of 32 up to %d dividing cols %d "
                      "(at most %d)", blk, kGvMaxBlk, cols, kGvMaxCols);
   if (!valid_dtype(w_dtype)) return set_error(ctx, FFAI_ATTN_ERR_INVALID, "unknown weight dtype");
-  if (!w || !qw || !bscale || !corr)
+  if (!w || !packed || !corr)
     return set_error(ctx, FFAI_ATTN_ERR_INVALID, "int8 GEMV quantize: null pointer");
   DeviceGuard g(ctx->device);
-  FFAI_CUDA(ctx, launch_int8_quantize(w, w_dtype, rows, cols, blk, qw, bscale, corr,
-                                      static_cast<cudaStream_t>(stream)));
+  FFAI_CUDA(ctx, launch_int8_quantize(w, w_dtype, rows, cols, blk, static_cast<uint8_t*>(packed),
+                                      corr, static_cast<cudaStream_t>(stream)));
   return FFAI_ATTN_OK;
 }
 
-int ffai_int8_gemv(ffai_attn_ctx* ctx, const float* x, int32_t batch, const int8_t* qw,
-                   const float* bscale, const float* corr, int32_t rows, int32_t cols,
-                   int32_t blk, float* out, uint32_t flags, void* stream) {
+int ffai_int8_gemv(ffai_attn_ctx* ctx, const float* x, int32_t batch, const void* packed,
+                   const float* corr, int32_t rows, int32_t cols, int32_t blk, float* out,
+                   uint32_t flags, void* stream) {
   if (!ctx) return set_error(nullptr, FFAI_ATTN_ERR_INVALID, "null context");
   if (flags & ~FFAI_INT8_FLAG_WEIGHTS_STABLE)
     return set_error(ctx, FFAI_ATTN_ERR_INVALID, "int8 GEMV: unknown flags 0x%x", flags);
@@ -1415,20 +1417,24 @@ int ffai_int8_gemv(ffai_attn_ctx* ctx, const float* x, int32_t batch, const int8
   if (batch < 1 || batch > kGvMaxBatch)
     return set_error(ctx, FFAI_ATTN_ERR_INVALID, "int8 GEMV: batch %d not in [1, %d]", batch,
                      kGvMaxBatch);
-  if (!x || !qw || !bscale || !corr || !out)
+  if (!x || !packed || !corr || !out)
     return set_error(ctx, FFAI_ATTN_ERR_INVALID, "int8 GEMV: null pointer");
-  for (const void* ptr : {static_cast<const void*>(qw), static_cast<const void*>(bscale)})
-    if (reinterpret_cast<uintptr_t>(ptr) % 16 != 0)
-      return set_error(ctx, FFAI_ATTN_ERR_INVALID, "int8 GEMV: weights and scales 16-byte aligned");
+  if (reinterpret_cast<uintptr_t>(packed) % 16 != 0 || reinterpret_cast<uintptr_t>(x) % 16 != 0)
+    return set_error(ctx, FFAI_ATTN_ERR_INVALID,
+                     "int8 GEMV: packed weights and activations 16-byte aligned");
   Int8GemvParams p{};
   if (!int8_gemv_plan(rows, cols, blk, batch, ctx->num_sms, &p.plan))
     return set_error(ctx, FFAI_ATTN_DECLINED, "int8 GEMV: no shared-memory plan for %d x %d",
                      rows, cols);
   DeviceGuard g(ctx->device);
+  constexpr size_t kXqBytes = static_cast<size_t>(kGvMaxCols) / 16 * 128;
+  int st = ensure(ctx, &ctx->d_gemv_x, &ctx->gemv_x_cap, kXqBytes + kGvMaxBatch * sizeof(float));
+  if (st) return st;
+  p.xq = ctx->d_gemv_x;
+  p.sx = reinterpret_cast<float*>(ctx->d_gemv_x + kXqBytes);
   p.x = x;
   p.batch = batch;
-  p.qw = qw;
-  p.bscale = bscale;
+  p.packed = static_cast<const uint8_t*>(packed);
   p.corr = corr;
   p.rows = rows;
   p.cols = cols;

@@ -13,21 +13,26 @@
 //     in [-64, 63] + 64, a 7-bit unsigned value -- cpu_fwd, :218-258;
 //   out = (sum_b f32(blocksum_b(xu * q)) * scale_b  -  corr) * sx, the sum
 //     taken in block order in f32 with separate multiply and add --
-//     dot_i8_blocked, :280-305.  The integer block sums are exact (dp4a).
+//     dot_i8_blocked, :280-305.
 //
 // B200 layout: the projection streams the whole weight matrix once per token
-// (75 MB for 51865 x 1280), so it is HBM-bound.  Because the f32 sum over a
-// row's blocks must run in block order, one lane owns one weight row and walks
-// its blocks in order; the weights are stored packed (kernels.h) so that the
-// 32 lanes of a warp read their 32 rows' next 16 bytes as one conflict-free
-// 512-byte shared-memory access.  Persistent CTAs, one per SM, each take a
-// contiguous range of 32-row groups; a producer warp streams the groups'
-// columns through a ring of shared-memory slots with 1-d bulk copies (weights
-// and block scales of a step are contiguous in the packed layout), and all
-// activation rows of the step (beams, up to 8) share that one pass.  Where a
-// CTA has few groups (the MLP's 1280-row fc2), the 16 consumer warps split
-// each group's blocks; their block products go through shared memory to the
-// warp that adds them in order.
+// (75 MB for 51865 x 1280), so it is HBM-bound.  The integer block sums are
+// exact on the tensor cores (mma.sync m16n8k32, s8 weights x u8 activations
+// -> s32; the activation rows of a step -- beams, up to 8 -- are the 8
+// columns), which leaves the SIMT pipes the reference's f32 epilogue: per
+// block, convert and multiply by the row's scale (any warp), then add in
+// block order (one warp per 16 rows, in registers).
+//
+// Streaming: persistent CTAs, one per SM, each take a contiguous range of
+// 32-row groups, cut into units of S block records (weights and their scales
+// are contiguous in the packed layout, so a unit is ONE bulk copy).  Units
+// go through a ring of shared-memory slots, each refilled by its own
+// producer lane: bulk copies issued by one thread complete one after
+// another, so a ring only turns into bytes in flight when every slot has its
+// own issuing thread.  Fourteen compute warps share every unit (two m16
+// tiles x S blocks) and leave the f32 block products in the slot, over the
+// weights they came from; two summing warps add them in block order and
+// hand the slot back to its producer lane.
 #include <algorithm>
 #include <atomic>
 
@@ -38,36 +43,48 @@ namespace ffai {
 
 namespace {
 
-constexpr int kGvWarps = 16;
-constexpr int kGvThreads = (kGvWarps + 1) * 32;  // + the producer warp
-constexpr int kGvCons = kGvWarps * 32;
-constexpr int kGvMaxStages = 6;
-constexpr int kGvStageBudget = 40960;  // target bytes per ring slot
+constexpr int kGvConsWarps = 16;
+constexpr int kGvThreads = (kGvConsWarps + 1) * 32;  // + the producer warp
+constexpr int kGvCons = kGvConsWarps * 32;
+#ifndef FFAI_GV_SLOT_TARGET
+#define FFAI_GV_SLOT_TARGET 24576
+#endif
+#ifndef FFAI_GV_RING_MAX
+#define FFAI_GV_RING_MAX 12
+#endif
+constexpr int kGvSlotTarget = FFAI_GV_SLOT_TARGET;  // bytes per slot to aim for
+constexpr int kGvMaxRing = FFAI_GV_RING_MAX;        // slots, one producer lane each
+constexpr int kGvComputeWarps = kGvConsWarps - 2;  // + two summing warps
+constexpr int kGvBlockStride = kGvComputeWarps / 2;  // blocks between a warp's blocks
 // Dynamic shared memory the kernel may use (227 KB per block, less a little
 // for its static arrays).
 constexpr int kGvSmemMax = 227 * 1024 - 1024;
 constexpr int kGvBarX = 1;  // named barrier of the activation quantisation
+#ifndef FFAI_GV_BATCH
+#define FFAI_GV_BATCH 3
+#endif
+constexpr int kGvBatch = FFAI_GV_BATCH;  // blocks whose mmas are in flight together
 
 // One warp per row: block scales, int8 weights and the row's correction term
-// in the reference's order of operations, written in the packed layout.
-// Warps past `rows` (up to the group boundary) write the zero padding.
+// in the reference's order of operations, written as block records.  Warps
+// past `rows` (up to the group boundary) write the zero padding.
 template <typename T>
 __global__ void __launch_bounds__(256) int8_quantize_kernel(const T* w, int rows, int cols, int blk,
-                                                            int8_t* qw, float* bscale,
-                                                            float* corr) {
+                                                            uint8_t* packed, float* corr) {
   const int row = (blockIdx.x * blockDim.x + threadIdx.x) / 32;
   const int lane = threadIdx.x % 32;
   const int padded = static_cast<int>(int8_gemv_groups(rows)) * 32;
   if (row >= padded) return;
-  const int g = row / 32, l = row % 32, nb = cols / blk, nc = cols / 16;
-  // byte column k of this row in the packed layout
-  auto qidx = [&](int k) {
-    return ((static_cast<size_t>(g) * nc + k / 16) * 32 + l) * 16 + k % 16;
-  };
-  auto sidx = [&](int b) { return (static_cast<size_t>(g) * nb + b) * 32 + l; };
+  const int g = row / 32, l = row % 32, nb = cols / blk, rec = int8_gemv_record(blk);
+  auto record = [&](int b) { return packed + (static_cast<size_t>(g) * nb + b) * rec; };
+  // column k (within block b) of this row
+  auto qbyte = [&](int b, int k) { return record(b) + ((k / 16) * 32 + l) * 16 + k % 16; };
+  auto scale = [&](int b) { return reinterpret_cast<float*>(record(b) + blk * 32) + l; };
   if (row >= rows) {
-    for (int k = lane; k < cols; k += 32) qw[qidx(k)] = 0;
-    for (int b = lane; b < nb; b += 32) bscale[sidx(b)] = 0.f;
+    for (int b = 0; b < nb; ++b) {
+      for (int k = lane; k < blk; k += 32) *qbyte(b, k) = 0;
+      if (lane == 0) *scale(b) = 0.f;
+    }
     if (lane == 0) corr[row] = 0.f;
     return;
   }
@@ -81,215 +98,302 @@ __global__ void __launch_bounds__(256) int8_quantize_kernel(const T* w, int rows
     const float sc = amax > 0.f ? __fdiv_rn(amax, 127.0f) : 1.0f;
     int bsum = 0;
     for (int k = lane; k < blk; k += 32) {
-      float r = roundf(__fdiv_rn(to_f32(src[b * blk + k]), sc));  // half away from zero
-      r = fminf(fmaxf(r, -127.0f), 127.0f);
-      const int qi = static_cast<int>(r);
-      qw[qidx(b * blk + k)] = static_cast<int8_t>(qi);
+      const float r = roundf(__fdiv_rn(to_f32(src[b * blk + k]), sc));  // half away from zero
+      // NaN -> 0, as Rust's saturating `as` cast after clamp
+      const int qi = r == r ? static_cast<int>(fminf(fmaxf(r, -127.0f), 127.0f)) : 0;
+      *qbyte(b, k) = static_cast<uint8_t>(static_cast<int8_t>(qi));
       bsum += qi;
     }
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) bsum += __shfl_xor_sync(0xffffffffu, bsum, o);
     c = __fadd_rn(c, __fmul_rn(sc, static_cast<float>(bsum)));
-    if (lane == 0) bscale[sidx(b)] = sc;
+    if (lane == 0) *scale(b) = sc;
   }
   if (lane == 0) corr[row] = __fmul_rn(64.0f, c);
 }
 
-// NB: activation rows handled (a power of two >= p.batch, <= 8).
-template <int NB>
+__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2,
+                                        uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(addr));
+}
+__device__ __forceinline__ void ldsm_x2(uint32_t addr, uint32_t& r0, uint32_t& r1) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x2.shared.b16 {%0, %1}, [%2];"
+               : "=r"(r0), "=r"(r1)
+               : "r"(addr));
+}
+// d += a (16 x 32, s8, row-major) * b (32 x 8, u8, column-major), exact s32.
+__device__ __forceinline__ void mma_s8u8(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2,
+                                         uint32_t a3, uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k32.row.col.s32.s8.u8.s32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, "
+      "{%8, %9}, {%0, %1, %2, %3};"
+      : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+// f32 of an integer block sum, exact: through the float 1.5 * 2^23 + s when
+// |s| < 2^22 (blocks of up to 256 columns: |s| <= 256 * 127 * 127), else by
+// conversion.
+template <bool SMALL>
+__device__ __forceinline__ float sum_to_f32(int s) {
+  if (SMALL) return __fsub_rn(__int_as_float(0x4B400000 + s), 12582912.0f);
+  return __int2float_rn(s);
+}
+
+// round(x / sx) as the reference computes it -- the IEEE quotient, rounded
+// half away from zero -- clamped to [-64, 63].  With fast_ok the approximate
+// quotient q is within 2 ulp of x / sx, so within 3 ulp of the IEEE
+// quotient; |q| <= 64 (|x| <= 63 sx), where 3 ulp < 3e-5.  A q more than
+// 6.4e-5 from every rounding boundary k + 1/2 therefore rounds like the IEEE
+// quotient; closer (or not finite), the IEEE division decides.  A NaN
+// quotient gives 0, as Rust's saturating `as` cast does.
+__device__ __forceinline__ int quant_act(float x, float sx, bool fast_ok) {
+  float q = __fdividef(x, sx);
+  const float a = fabsf(q);
+  const float dist = fabsf((a - floorf(a)) - 0.5f);
+  if (!(fast_ok && dist > 6.4e-5f)) q = __fdiv_rn(x, sx);
+  if (q != q) return 0;
+  return static_cast<int>(fminf(fmaxf(roundf(q), -64.0f), 63.0f));
+}
+
+// Activations, once per GEMV: CTA b quantises row b of x -- amax over the
+// row, sx = amax / 63 (1 when zero), xu = round(x / sx) + 64 -- into the
+// layout the GEMV's ldmatrix reads: xq[(c * 8 + b) * 16 + j] = xu of column
+// 16 c + j; CTA 0 also zeroes the rows past the batch.
+constexpr int kActThreads = 256;
+__global__ void __launch_bounds__(kActThreads) int8_act_kernel(const float* x, int B, int cols,
+                                                               uint8_t* xq, float* sx_out) {
+  __shared__ float s_red[kActThreads / 32];
+  __shared__ float s_sx;
+  griddep_launch_dependents();
+  griddep_wait();  // x comes from the preceding kernel
+  const int b = blockIdx.x, tid = threadIdx.x, c4 = cols / 4;
+  const float4* xr = reinterpret_cast<const float4*>(x + static_cast<size_t>(b) * cols);
+  constexpr int kRegs = kGvMaxCols / 4 / kActThreads;
+  float4 v[kRegs];
+  float m = 0.f;
+#pragma unroll
+  for (int j = 0; j < kRegs; ++j) {
+    const int i = tid + j * kActThreads;
+    if (i < c4) {
+      v[j] = __ldg(xr + i);
+      m = fmaxf(fmaxf(fmaxf(m, fabsf(v[j].x)), fabsf(v[j].y)), fmaxf(fabsf(v[j].z), fabsf(v[j].w)));
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+  if (tid % 32 == 0) s_red[tid / 32] = m;
+  __syncthreads();
+  if (tid == 0) {
+    float a = 0.f;
+    for (int w = 0; w < kActThreads / 32; ++w) a = fmaxf(a, s_red[w]);
+    s_sx = a > 0.f ? __fdiv_rn(a, 63.0f) : 1.0f;
+    sx_out[b] = s_sx;
+  }
+  __syncthreads();
+  const float sx = s_sx;
+  // sx well inside the normal range: the approximate quotient is good to 2 ulp
+  const bool fast_ok = sx >= 0x1p-120f && sx <= 0x1p120f;
+  uint32_t* xw = reinterpret_cast<uint32_t*>(xq);
+#pragma unroll
+  for (int j = 0; j < kRegs; ++j) {
+    const int i = tid + j * kActThreads;
+    if (i < c4) {
+      const float e[4] = {v[j].x, v[j].y, v[j].z, v[j].w};
+      uint32_t word = 0;
+#pragma unroll
+      for (int t = 0; t < 4; ++t)
+        word |= static_cast<uint32_t>(quant_act(e[t], sx, fast_ok) + 64) << (8 * t);
+      const int col = 4 * i;
+      xw[((col >> 4) * 8 + b) * 4 + ((col >> 2) & 3)] = word;
+    }
+  }
+  if (b == 0) {
+    const int nc = cols / 16;
+    for (int w = tid; w < nc * 32; w += kActThreads)
+      if (((w >> 2) & 7) >= B) xw[w] = 0u;
+  }
+}
+
+template <bool SMALL>
 __global__ void __launch_bounds__(kGvThreads, 1) int8_gemv_kernel(Int8GemvParams p) {
   const Int8GemvPlan& P = p.plan;
   extern __shared__ __align__(128) uint8_t dsm[];
   uint8_t* xq = dsm + P.x_off;
-  float* prod = reinterpret_cast<float*>(dsm + P.p_off);
   uint64_t* full = reinterpret_cast<uint64_t*>(dsm + P.bar_off);
-  uint64_t* empty = full + kGvMaxStages;
-  uint64_t* gbar = empty + kGvMaxStages;  // per group of a round: products ready
+  uint64_t* ready = full + kGvMaxRing;   // compute warps wrote the slot's products
+  uint64_t* empty = ready + kGvMaxRing;  // summing warps read them
   __shared__ float s_sx[kGvMaxBatch];
-  __shared__ float s_red[kGvMaxBatch][kGvWarps];
   __shared__ int s_abort;
 
   const int tid = threadIdx.x, warp = tid / 32, lane = tid % 32;
   const int cols = p.cols, blk = p.blk, B = p.batch;
-  const int nb = cols / blk, gc = blk / 16, nc = cols / 16;
-  const int S = P.S, nmax = P.nmax, wpg = P.wpg, stages = P.stages;
-  const int steps = (nb + S - 1) / S;
+  const int nb = cols / blk, gc = blk / 16, nc = cols / 16, rec = int8_gemv_record(blk);
+  const int S = P.S, ring = P.ring;
+  const int upg = (nb + S - 1) / S;  // units (slot loads) per group
   const int g_begin = static_cast<int>(static_cast<long long>(blockIdx.x) * P.groups / P.grid);
   const int g_end = static_cast<int>(static_cast<long long>(blockIdx.x + 1) * P.groups / P.grid);
-  const int w_slot = nmax * S * blk * 32;  // weight bytes of a slot; scales follow
+  const int units = (g_end - g_begin) * upg;
 
   if (tid == 0) {
-    for (int i = 0; i < stages; ++i) {
+    for (int i = 0; i < ring; ++i) {
       mbar_init(&full[i], 1);
-      mbar_init(&empty[i], kGvWarps);
+      mbar_init(&ready[i], kGvComputeWarps);
+      mbar_init(&empty[i], 2);
     }
-    for (int i = 0; i < nmax; ++i) mbar_init(&gbar[i], wpg);
     s_abort = 0;
     fence_mbar_init();
   }
   __syncthreads();
   griddep_launch_dependents();
 
-  // Producer: per round and step, the S-block column range of each group
-  // (weights, then scales), one pair of bulk copies per group.  Stable
-  // weights stream while the preceding kernel finishes; the activations come
-  // from it, so the consumers always wait for it.
-  if (warp == kGvWarps) {
+  // Producer: lane r refills slot r with units r, r + ring, ... (unit u =
+  // group u / upg of the CTA, blocks [k S, k S + S) with k = u % upg), each
+  // ONE bulk copy.  Stable weights stream while the preceding kernel
+  // finishes; the activations come from it, so the consumers always wait.
+  if (warp == kGvConsWarps) {
     if (!p.weights_stable) griddep_wait();
-    int seq = 0;
+    if (lane >= ring) return;
+    uint64_t* fb = &full[lane];
+    int issued = 0;
     bool ok = true;
-    for (int g0 = g_begin; g0 < g_end && ok; g0 += nmax) {
-      const int n = min(nmax, g_end - g0);
-      for (int k = 0; k < steps; ++k, ++seq) {
-        const int st = seq % stages;
-        if (seq >= stages) {
-          int got = 1;
-          if (lane == 0)
-            got = mbar_wait(&empty[st], ((seq / stages) - 1) & 1, &s_abort, p.err,
-                            kErrTimeoutProducer);
-          if (!__shfl_sync(0xffffffffu, got, 0)) {
-            ok = false;
-            break;
-          }
-        }
-        const int sk = min(S, nb - k * S);
-        if (lane == 0)
-          mbar_arrive_expect_tx(&full[st], static_cast<uint32_t>(n) * sk * (blk * 32 + 128));
-        __syncwarp();
-        if (lane < n) {
-          const size_t g = static_cast<size_t>(g0 + lane);
-          uint8_t* slot = dsm + static_cast<size_t>(st) * P.slot_bytes;
-          bulk_load(slot + static_cast<size_t>(lane) * S * blk * 32,
-                    p.qw + (g * nc + static_cast<size_t>(k) * S * gc) * 512,
-                    static_cast<uint32_t>(sk) * blk * 32, &full[st]);
-          bulk_load(slot + w_slot + static_cast<size_t>(lane) * S * 128,
-                    p.bscale + (g * nb + static_cast<size_t>(k) * S) * 32,
-                    static_cast<uint32_t>(sk) * 128, &full[st]);
-        }
-      }
-    }
-    if (!ok && lane == 0) {
-      // Let the copies in flight land before the CTA exits.
-      int none = 0;
-      for (int i = 0; i < stages && i < seq; ++i) {
-        const int arms = (seq - 1 - i) / stages + 1;
-        mbar_wait(&full[i], (arms - 1) & 1, &none, p.err, kErrTimeoutDrain);
-      }
-    }
-    return;  // the producer takes no part in the barriers below
-  }
-
-  // Activations: per row b, sx = amax / 63 and xu = round(x / sx) + 64, once
-  // per CTA into shared memory.
-  griddep_wait();
-  for (int b = 0; b < B; ++b) {
-    const float* xr = p.x + static_cast<size_t>(b) * cols;
-    float amax = 0.f;
-    for (int k = tid; k < cols; k += kGvCons) amax = fmaxf(amax, fabsf(xr[k]));
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
-    if (lane == 0) s_red[b][warp] = amax;
-  }
-  named_bar_sync(kGvBarX, kGvCons);
-  if (tid < B) {
-    float m = 0.f;
-    for (int w = 0; w < kGvWarps; ++w) m = fmaxf(m, s_red[tid][w]);
-    s_sx[tid] = m > 0.f ? __fdiv_rn(m, 63.0f) : 1.0f;
-  }
-  named_bar_sync(kGvBarX, kGvCons);
-  for (int i = tid; i < B * cols; i += kGvCons) {
-    const int b = i / cols;
-    float r = roundf(__fdiv_rn(p.x[i], s_sx[b]));
-    r = fminf(fmaxf(r, -64.0f), 63.0f);
-    xq[i] = static_cast<uint8_t>(static_cast<int>(r) + 64);
-  }
-  named_bar_sync(kGvBarX, kGvCons);
-
-  // Consumers: warp w works on group gi = w / wpg of each round, on the
-  // blocks j, j + wpg, ... (j = w % wpg) of each step; lane l is row 32g + l.
-  const int gi = warp / wpg, j = warp % wpg;
-  int seq = 0, buf = 0, gphase = 0;
-  bool ok = true;
-  for (int g0 = g_begin; g0 < g_end && ok; g0 += nmax) {
-    const int n = min(nmax, g_end - g0);
-    const bool active = gi < n;
-    float acc[NB];
-#pragma unroll
-    for (int b = 0; b < NB; ++b) acc[b] = 0.f;
-    for (int k = 0; k < steps; ++k, ++seq) {
-      const int st = seq % stages;
-      if (!mbar_wait(&full[st], (seq / stages) & 1, &s_abort, p.err, kErrTimeoutConsumer)) {
+    for (int u = lane; u < units; u += ring) {
+      if (issued > 0 &&
+          !mbar_wait(&empty[lane], (issued - 1) & 1, &s_abort, p.err, kErrTimeoutProducer)) {
         ok = false;
         break;
       }
-      const int sk = min(S, nb - k * S);
-      if (active) {
-        const uint8_t* ws = dsm + static_cast<size_t>(st) * P.slot_bytes +
-                            static_cast<size_t>(gi) * S * blk * 32;
-        const float* ss = reinterpret_cast<const float*>(dsm + static_cast<size_t>(st) * P.slot_bytes +
-                                                         w_slot) + gi * S * 32;
-        for (int kb = j; kb < sk; kb += wpg) {
-          int is[NB];
-#pragma unroll
-          for (int b = 0; b < NB; ++b) is[b] = 0;
-          const int c0 = (k * S + kb) * gc;  // first column chunk of the block
-#pragma unroll 2
-          for (int ch = 0; ch < gc; ++ch) {
-            const uint4 wv = *reinterpret_cast<const uint4*>(ws + ((kb * gc + ch) * 32 + lane) * 16);
-#pragma unroll
-            for (int b = 0; b < NB; ++b) {
-              if (b < B) {
-                const uint4 xv = *reinterpret_cast<const uint4*>(xq + b * cols + (c0 + ch) * 16);
-                int s = __dp4a(static_cast<int>(wv.x), static_cast<int>(xv.x), is[b]);
-                s = __dp4a(static_cast<int>(wv.y), static_cast<int>(xv.y), s);
-                s = __dp4a(static_cast<int>(wv.z), static_cast<int>(xv.z), s);
-                is[b] = __dp4a(static_cast<int>(wv.w), static_cast<int>(xv.w), s);
-              }
-            }
-          }
-          const float sc = ss[kb * 32 + lane];
-#pragma unroll
-          for (int b = 0; b < NB; ++b) {
-            if (b < B) {
-              const float pr = __fmul_rn(__int2float_rn(is[b]), sc);
-              if (wpg == 1)
-                acc[b] = __fadd_rn(acc[b], pr);
-              else
-                prod[((((buf * nmax + gi) * S + kb) * B + b) * 32) + lane] = pr;
-            }
-          }
-        }
-      }
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&empty[st]);
-      if (wpg > 1 && active) {
-        // Every warp of the group has written its products of this step:
-        // warp j adds, in block order, those of the beams b = j (mod wpg).
-        if (lane == 0) mbar_arrive(&gbar[gi]);
-        if (!mbar_wait(&gbar[gi], gphase & 1, &s_abort, p.err, kErrTimeoutConsumer)) {
-          ok = false;
-          break;
-        }
-        ++gphase;
-#pragma unroll
-        for (int b = 0; b < NB; ++b) {
-          if (b < B && b % wpg == j) {
-            const float* src = prod + (((buf * nmax + gi) * S) * B + b) * 32 + lane;
-            for (int kb = 0; kb < sk; ++kb) acc[b] = __fadd_rn(acc[b], src[kb * B * 32]);
-          }
-        }
-        buf ^= 1;
-      }
+      const int k = u % upg;
+      const size_t g = static_cast<size_t>(g_begin + u / upg);
+      const uint32_t bytes = static_cast<uint32_t>(min(S, nb - k * S)) * rec;
+      mbar_arrive_expect_tx(fb, bytes);
+      bulk_load(dsm + static_cast<size_t>(lane) * P.slot_bytes,
+                p.packed + (g * nb + static_cast<size_t>(k) * S) * rec, bytes, fb);
+      ++issued;
     }
-    if (ok && active) {
-      const int row = (g0 + gi) * 32 + lane;
-      if (row < p.rows) {
-        const float cr = __ldg(p.corr + row);
+    if (issued > 0 && (!ok || s_abort)) {
+      // Let this slot's last copy land before the CTA exits.
+      int none = 0;
+      mbar_wait(fb, (issued - 1) & 1, &none, p.err, kErrTimeoutDrain);
+    }
+    return;
+  }
+
+  // Activations, quantised by int8_act_kernel just before (the preceding
+  // kernel): xq [chunk of 16 columns][8 rows][16 bytes] -- the mma's B
+  // operand, 8 x 16 bytes per ldmatrix -- and sx per row.
+  griddep_wait();
+  {
+    const uint4* src = reinterpret_cast<const uint4*>(p.xq);
+    uint4* dst = reinterpret_cast<uint4*>(xq);
+    for (int i = tid; i < nc * 8; i += kGvCons) dst[i] = src[i];
+    if (tid < B) s_sx[tid] = p.sx[tid];
+  }
+  named_bar_sync(kGvBarX, kGvCons);
+
+  // Consumers.  Compute warps c = 0 .. 13 take m16 tile c & 1 (rows
+  // 16 (c & 1) ..) of blocks c / 2, c / 2 + 7, ... of every unit and write
+  // the f32 block products over the weights they have just read (16 rows x
+  // 16 bytes of the block's first two chunks: 512 bytes, one float4 a lane).
+  // Warps 14 and 15 add a unit's products in block order for tile 0 / 1,
+  // keeping a group's sums in registers, and release the slot.
+  const int gq = lane >> 2, tig = lane & 3;
+  if (warp < kGvComputeWarps) {
+    const int mt = warp & 1, kb0 = warp >> 1;
+    // ldmatrix row addresses: A -- lanes 8j..8j+7 give rows of matrix j
+    // (j = 0, 1: chunk 2s, rows 0-7 / 8-15; j = 2, 3: chunk 2s + 1);
+    // B -- lanes 0-7 / 8-15 give the 8 activation rows of chunk 2s / 2s + 1.
+    const uint32_t a_lane = (((lane >> 4) * 32) + (lane & 7) + ((lane >> 3) & 1) * 8 + 16 * mt) * 16;
+    const uint32_t b_lane = ((((lane >> 3) & 1) * 8) + (lane & 7)) * 16;
+    const uint32_t prod_lane = (lane >> 4) * 512 + mt * 256 + (lane & 15) * 16;
+    const uint32_t xq_s = smem_u32(xq), dsm_s = smem_u32(dsm);
+    for (int u = 0; u < units; ++u) {
+      const int k = u % upg, r = u % ring;
+      if (!mbar_wait(&full[r], (u / ring) & 1, &s_abort, p.err, kErrTimeoutConsumer)) break;
+      const int sk = min(S, nb - k * S);
+      const uint32_t slot_s = dsm_s + r * P.slot_bytes;
+      for (int kbb = kb0; kbb < sk; kbb += kGvBlockStride * kGvBatch) {
+        int d[kGvBatch][4];
+        uint32_t rec_s[kGvBatch], x_s[kGvBatch];
 #pragma unroll
-        for (int b = 0; b < NB; ++b)
-          if (b < B && b % wpg == j)
-            p.out[static_cast<size_t>(b) * p.rows + row] = __fmul_rn(__fsub_rn(acc[b], cr), s_sx[b]);
+        for (int i = 0; i < kGvBatch; ++i) {
+          // past the end: a valid block, result unused
+          const int kb = min(kbb + kGvBlockStride * i, sk - 1);
+          rec_s[i] = slot_s + kb * rec;
+          x_s[i] = xq_s + static_cast<uint32_t>((k * S + kb) * gc) * 128;
+#pragma unroll
+          for (int j = 0; j < 4; ++j) d[i][j] = 0;
+        }
+        for (int sl = 0; sl < gc / 2; ++sl) {
+          uint32_t a[kGvBatch][4], bx[kGvBatch][2];
+#pragma unroll
+          for (int i = 0; i < kGvBatch; ++i) {
+            ldsm_x4(rec_s[i] + sl * 1024 + a_lane, a[i][0], a[i][1], a[i][2], a[i][3]);
+            ldsm_x2(x_s[i] + sl * 256 + b_lane, bx[i][0], bx[i][1]);
+          }
+#pragma unroll
+          for (int i = 0; i < kGvBatch; ++i)
+            mma_s8u8(d[i], a[i][0], a[i][1], a[i][2], a[i][3], bx[i][0], bx[i][1]);
+        }
+#pragma unroll
+        for (int i = 0; i < kGvBatch; ++i) {
+          if (kbb + kGvBlockStride * i < sk) {
+            uint8_t* recp = dsm + (rec_s[i] - dsm_s);
+            const float* sc = reinterpret_cast<const float*>(recp + blk * 32) + 16 * mt + gq;
+            const float s0 = sc[0], s1 = sc[8];
+            *reinterpret_cast<float4*>(recp + prod_lane) =
+                make_float4(__fmul_rn(sum_to_f32<SMALL>(d[i][0]), s0),
+                            __fmul_rn(sum_to_f32<SMALL>(d[i][1]), s0),
+                            __fmul_rn(sum_to_f32<SMALL>(d[i][2]), s1),
+                            __fmul_rn(sum_to_f32<SMALL>(d[i][3]), s1));
+          }
+        }
       }
+      fence_proxy_async_smem();  // the slot is refilled by a bulk copy after the summers read it
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&ready[r]);
+    }
+    return;
+  }
+
+  // Summing warps: tile st of every unit, the products in block order.
+  const int st = warp - kGvComputeWarps;
+  const uint32_t prod_lane = (lane >> 4) * 512 + st * 256 + (lane & 15) * 16;
+  float acc[4] = {0.f, 0.f, 0.f, 0.f};
+  for (int u = 0; u < units; ++u) {
+    const int li = u / upg, k = u - li * upg, r = u % ring;
+    if (!mbar_wait(&ready[r], (u / ring) & 1, &s_abort, p.err, kErrTimeoutConsumer)) break;
+    const int sk = min(S, nb - k * S);
+    const uint8_t* src = dsm + static_cast<size_t>(r) * P.slot_bytes + prod_lane;
+    for (int kb = 0; kb < sk; ++kb) {
+      const float4 v = *reinterpret_cast<const float4*>(src + kb * rec);
+      acc[0] = __fadd_rn(acc[0], v.x);
+      acc[1] = __fadd_rn(acc[1], v.y);
+      acc[2] = __fadd_rn(acc[2], v.z);
+      acc[3] = __fadd_rn(acc[3], v.w);
+    }
+    fence_proxy_async_smem();
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&empty[r]);
+    if (k == upg - 1) {
+      // thread (gq, tig) holds rows gq, gq + 8 of tile st, beams 2 tig, 2 tig + 1
+      const int r0 = (g_begin + li) * 32 + 16 * st + gq, r1 = r0 + 8;
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        const int b = 2 * tig + e;
+        if (b >= B) continue;
+        const float sx = s_sx[b];
+        if (r0 < p.rows)
+          p.out[static_cast<size_t>(b) * p.rows + r0] =
+              __fmul_rn(__fsub_rn(acc[e], __ldg(p.corr + r0)), sx);
+        if (r1 < p.rows)
+          p.out[static_cast<size_t>(b) * p.rows + r1] =
+              __fmul_rn(__fsub_rn(acc[2 + e], __ldg(p.corr + r1)), sx);
+      }
+#pragma unroll
+      for (int j = 0; j < 4; ++j) acc[j] = 0.f;
     }
   }
 }
@@ -303,45 +407,38 @@ bool int8_gemv_plan(int rows, int cols, int blk, int batch, int sms, Int8GemvPla
   const long long groups = int8_gemv_groups(rows);
   P.groups = static_cast<int>(groups);
   P.grid = static_cast<int>(std::min<long long>(sms, groups));
-  const int per_gb = blk * 32 + 128;  // one block of one group: weights and scales
-  const int per_cta = static_cast<int>((groups + P.grid - 1) / P.grid);
-  P.nmax = std::min(kGvWarps, per_cta);
-  P.nmax = std::min(P.nmax, std::max(1, kGvStageBudget / per_gb));
-  P.wpg = std::max(1, kGvWarps / P.nmax);
-  const int nb = cols / blk;
-  P.S = std::min(nb, std::max(1, kGvStageBudget / (P.nmax * per_gb)));
-  if (P.wpg > 1 && P.S >= P.wpg) P.S = P.S / P.wpg * P.wpg;
-  P.slot_bytes = P.nmax * P.S * per_gb;
-  const int x_bytes = (batch * cols + 127) / 128 * 128;
-  const int p_bytes = P.wpg > 1 ? 2 * P.nmax * P.S * batch * 128 : 0;
-  const int bar_bytes = (2 * kGvMaxStages + kGvWarps) * 8;
-  const int avail = kGvSmemMax - x_bytes - p_bytes - bar_bytes;
-  P.stages = std::min(kGvMaxStages, avail / P.slot_bytes);
-  if (P.stages < 2) return false;
-  P.x_off = P.stages * P.slot_bytes;
-  P.p_off = P.x_off + x_bytes;
-  P.bar_off = P.p_off + p_bytes;
+  const int rec = int8_gemv_record(blk), nb = cols / blk;
+  const int upg = std::max(1, (nb * rec + kGvSlotTarget - 1) / kGvSlotTarget);
+  P.S = (nb + upg - 1) / upg;
+  P.slot_bytes = P.S * rec;
+  const int x_bytes = (cols / 16) * 128;
+  const int bar_bytes = 3 * kGvMaxRing * 8;
+  const int avail = kGvSmemMax - x_bytes - bar_bytes;
+  P.ring = std::min(kGvMaxRing, avail / P.slot_bytes);
+  if (P.ring < 2) return false;
+  P.x_off = P.ring * P.slot_bytes;
+  P.bar_off = P.x_off + x_bytes;
   P.smem = P.bar_off + bar_bytes;
   *plan = P;
   return true;
 }
 
 cudaError_t launch_int8_quantize(const void* w, int w_dtype, int rows, int cols, int blk,
-                                 int8_t* qw, float* bscale, float* corr, cudaStream_t s) {
+                                 uint8_t* packed, float* corr, cudaStream_t s) {
   const long long padded = int8_gemv_groups(rows) * 32;
   const int blocks = static_cast<int>((padded + 7) / 8);  // 8 warps of 32
   switch (w_dtype) {
     case 0:
       int8_quantize_kernel<float><<<blocks, 256, 0, s>>>(static_cast<const float*>(w), rows, cols,
-                                                         blk, qw, bscale, corr);
+                                                         blk, packed, corr);
       break;
     case 1:
       int8_quantize_kernel<__nv_bfloat16><<<blocks, 256, 0, s>>>(
-          static_cast<const __nv_bfloat16*>(w), rows, cols, blk, qw, bscale, corr);
+          static_cast<const __nv_bfloat16*>(w), rows, cols, blk, packed, corr);
       break;
     case 2:
       int8_quantize_kernel<__half><<<blocks, 256, 0, s>>>(static_cast<const __half*>(w), rows,
-                                                          cols, blk, qw, bscale, corr);
+                                                          cols, blk, packed, corr);
       break;
     default:
       return cudaErrorInvalidValue;
@@ -352,7 +449,7 @@ cudaError_t launch_int8_quantize(const void* w, int w_dtype, int rows, int cols,
 cudaError_t launch_int8_gemv(const Int8GemvParams& p, cudaStream_t s) {
   const Int8GemvPlan& P = p.plan;
   if (p.batch < 1 || p.batch > kGvMaxBatch || !int8_gemv_served(p.cols, p.blk) ||
-      P.smem > kGvSmemMax || P.stages < 2 || P.stages > kGvMaxStages || P.nmax > kGvWarps)
+      P.smem > kGvSmemMax || P.ring < 2 || P.ring > kGvMaxRing)
     return cudaErrorInvalidValue;
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
@@ -361,31 +458,34 @@ cudaError_t launch_int8_gemv(const Int8GemvParams& p, cudaStream_t s) {
   static std::atomic<bool> configured[64];
   if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
   if (!configured[dev].load(std::memory_order_acquire)) {
-    for (auto fn : {int8_gemv_kernel<1>, int8_gemv_kernel<2>, int8_gemv_kernel<4>,
-                    int8_gemv_kernel<8>}) {
+    for (auto fn : {int8_gemv_kernel<true>, int8_gemv_kernel<false>}) {
       e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, kGvSmemMax);
       if (e != cudaSuccess) return e;
     }
     configured[dev].store(true, std::memory_order_release);
   }
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cudaLaunchConfig_t acfg{};
+  acfg.gridDim = dim3(static_cast<unsigned>(p.batch));
+  acfg.blockDim = dim3(kActThreads);
+  acfg.stream = s;
+  acfg.attrs = attr;
+  acfg.numAttrs = 1;
+  e = cudaLaunchKernelEx(&acfg, int8_act_kernel, p.x, p.batch, p.cols, p.xq, p.sx);
+  if (e != cudaSuccess) return e;
   cudaLaunchConfig_t cfg{};
   cfg.gridDim = dim3(static_cast<unsigned>(P.grid));
   cfg.blockDim = dim3(kGvThreads);
   cfg.dynamicSmemBytes = static_cast<size_t>(P.smem);
   cfg.stream = s;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  if (p.batch <= 1)
-    e = cudaLaunchKernelEx(&cfg, int8_gemv_kernel<1>, p);
-  else if (p.batch <= 2)
-    e = cudaLaunchKernelEx(&cfg, int8_gemv_kernel<2>, p);
-  else if (p.batch <= 4)
-    e = cudaLaunchKernelEx(&cfg, int8_gemv_kernel<4>, p);
+  if (p.blk <= 256)
+    e = cudaLaunchKernelEx(&cfg, int8_gemv_kernel<true>, p);
   else
-    e = cudaLaunchKernelEx(&cfg, int8_gemv_kernel<8>, p);
+    e = cudaLaunchKernelEx(&cfg, int8_gemv_kernel<false>, p);
   if (e != cudaSuccess) return e;
   return cudaGetLastError();
 }

@@ -76,17 +76,20 @@ cudaError_t launch_kv_copy_pages(const DecodeParams& p, const int* src, const in
 
 // ---- int8 GEMV (gemv_int8.cu) ----------------------------------------------
 
-// Device layout of the quantised weights, G = ceil(rows / 32) groups of 32
-// rows (rows past `rows` are zero):
-//   qw     (G, cols / 16, 32, 16) int8: bytes [16c, 16c + 16) of row 32g + l
-//          at ((g * cols / 16 + c) * 32 + l) * 16, so lane l of a warp reads
-//          row 32g + l with conflict-free 16-byte loads;
-//   bscale (G, cols / blk, 32) f32: scale of block b of row 32g + l;
-//   corr   (G * 32) f32.
+// Device layout of the quantised weights: rows padded to G = ceil(rows / 32)
+// groups of 32 (padding zero); group g is nb = cols / blk block records in
+// column order, each kGvRecord(blk) = blk * 32 + 128 bytes:
+//   bytes [0, blk * 32): chunk c (16 columns) of the block for row l at
+//     (c * 32 + l) * 16 -- 32 rows x 16 bytes per chunk, so 8 rows of a chunk
+//     are one 128-byte matrix for ldmatrix;
+//   bytes [blk * 32, blk * 32 + 128): the 32 rows' f32 block scales.
+// A group's records are contiguous (group g at g * nb * record bytes), so
+// any run of a group's blocks is one bulk copy.  corr: (G * 32) f32.
 constexpr int kGvMaxBatch = 8;
 constexpr int kGvMaxCols = 8192;
 constexpr int kGvMaxBlk = 1024;
 
+__host__ __device__ inline int int8_gemv_record(int blk) { return blk * 32 + 128; }
 inline bool int8_gemv_served(int cols, int blk) {
   return blk > 0 && blk % 32 == 0 && blk <= kGvMaxBlk && cols > 0 && cols % blk == 0 &&
          cols <= kGvMaxCols;
@@ -94,32 +97,31 @@ inline bool int8_gemv_served(int cols, int blk) {
 __host__ __device__ inline long long int8_gemv_groups(long long rows) { return (rows + 31) / 32; }
 
 // Launch geometry, computed on the host.  CTA c takes the contiguous groups
-// [c * groups / grid, (c + 1) * groups / grid) in rounds of up to `nmax`
-// groups; `wpg` consumer warps share a group (each a subset of its blocks);
-// a round streams its groups' columns through the shared-memory ring in steps
-// of `S` blocks per group.
+// [c * groups / grid, (c + 1) * groups / grid), streamed as units of S block
+// records of one group through a ring of `ring` shared-memory slots.
 struct Int8GemvPlan {
-  int groups, grid, nmax, wpg, S, stages;
-  int slot_bytes;   // one ring slot: nmax * S * (blk * 32 + 128)
-  int x_off, p_off, bar_off, smem;
+  int groups, grid, ring, S;
+  int slot_bytes;  // S * record bytes
+  int x_off, bar_off, smem;
 };
 bool int8_gemv_plan(int rows, int cols, int blk, int batch, int sms, Int8GemvPlan* plan);
 
 struct Int8GemvParams {
-  const float* x;       // (batch, cols) f32 activations
-  int batch;            // 1..8
-  const int8_t* qw;     // packed weights (layout above)
-  const float* bscale;  // packed block scales
-  const float* corr;    // (G * 32) activation-offset corrections
-  int rows, cols, blk;  // int8_gemv_served(cols, blk)
-  float* out;           // (batch, rows)
+  const float* x;          // (batch, cols) f32 activations, 16-byte aligned
+  int batch;               // 1..8
+  uint8_t* xq;             // (cols / 16) * 128 bytes: quantised activations
+  float* sx;               // (8) activation scales
+  const uint8_t* packed;   // block records (layout above)
+  const float* corr;       // (G * 32) activation-offset corrections
+  int rows, cols, blk;     // int8_gemv_served(cols, blk)
+  float* out;              // (batch, rows)
   unsigned* err;
-  int weights_stable;   // weights not written by the preceding kernel
+  int weights_stable;      // weights not written by the preceding kernel
   Int8GemvPlan plan;
 };
 
 cudaError_t launch_int8_quantize(const void* w, int w_dtype, int rows, int cols, int blk,
-                                 int8_t* qw, float* bscale, float* corr, cudaStream_t s);
+                                 uint8_t* packed, float* corr, cudaStream_t s);
 cudaError_t launch_int8_gemv(const Int8GemvParams& p, cudaStream_t s);
 
 // ---- checked f32 prefill (prefill_simt.cu) ---------------------------------

@@ -7,8 +7,9 @@ projections -- the vocabulary projection and the MLP layers that reuse it
 None for a shape it does not serve (as `Int8Vocab::new` does);
 `forward(x)` maps (batch, cols) f32 activations (batch <= 8, e.g. the beams
 of a step) to (batch, rows) f32 in one pass over the weights.  The quantised
-weights live in the library's packed device layout; `unpacked()` returns
-them as the reference holds them (row-major q, (rows, nblocks) scales, corr).
+weights live in the library's device layout of block records (weights and
+scales of 32 rows x one block together); `unpacked()` returns them as the
+reference holds them (row-major q, (rows, nblocks) scales, corr).
 """
 
 from __future__ import annotations
@@ -33,16 +34,16 @@ def default_blk() -> int:
 
 
 def layout(rows: int, cols: int, blk: int):
-    """(qw bytes, scale count, corr count) of the packed layout, or None when
-    the shape is not served."""
-    n = [ctypes.c_int64(0) for _ in range(3)]
+    """(packed bytes, corr count) of the device layout, or None when the shape
+    is not served."""
+    n = [ctypes.c_int64(0) for _ in range(2)]
     st = _abi.load().ffai_int8_gemv_layout(rows, cols, blk, *(ctypes.byref(v) for v in n))
     return None if st != _abi.OK else tuple(v.value for v in n)
 
 
 class Int8Gemv:
-    def __init__(self, qw, bscale, corr, rows: int, cols: int, blk: int):
-        self.qw, self.bscale, self.corr = qw, bscale, corr
+    def __init__(self, packed, corr, rows: int, cols: int, blk: int):
+        self.packed, self.corr = packed, corr
         self.rows, self.cols, self.blk = rows, cols, blk
         # The first GEMV after the quantising kernel must not start streaming
         # the weights before that kernel ends; later ones may.
@@ -60,21 +61,23 @@ class Int8Gemv:
             return None
         w = w.contiguous()
         dev = w.device
-        qw = torch.empty(sizes[0], dtype=torch.int8, device=dev)
-        bscale = torch.empty(sizes[1], dtype=torch.float32, device=dev)
-        corr = torch.empty(sizes[2], dtype=torch.float32, device=dev)
+        packed = torch.empty(sizes[0], dtype=torch.uint8, device=dev)
+        corr = torch.empty(sizes[1], dtype=torch.float32, device=dev)
         ctx = context(dev.index)
         st = _abi.load().ffai_int8_gemv_quantize(ctx, _ptr(w), _DT[w.dtype], rows, cols, blk,
-                                                 _ptr(qw), _ptr(bscale), _ptr(corr), _stream(dev))
+                                                 _ptr(packed), _ptr(corr), _stream(dev))
         _check(st, ctx)
-        return cls(qw, bscale, corr, rows, cols, blk)
+        return cls(packed, corr, rows, cols, blk)
 
     def forward(self, x: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
         if x.dtype != torch.float32:  # as cpu_fwd (vocab_int8.rs:219-222)
             raise TypeError("int8 GEMV: f32 activations only")
-        if x.device != self.qw.device or x.shape[-1] != self.cols:
-            raise ValueError(f"int8 GEMV: activations must be (batch, {self.cols}) on {self.qw.device}")
+        if x.device != self.packed.device or x.shape[-1] != self.cols:
+            raise ValueError(
+                f"int8 GEMV: activations must be (batch, {self.cols}) on {self.packed.device}")
         x = x.reshape(-1, self.cols).contiguous()
+        if x.data_ptr() % 16:
+            x = x.clone()  # the kernel reads the activations as 16-byte vectors
         batch = x.shape[0]
         if out is None:
             out = torch.empty((batch, self.rows), dtype=torch.float32, device=x.device)
@@ -82,17 +85,22 @@ class Int8Gemv:
             raise ValueError(f"int8 GEMV: out must be contiguous f32 ({batch}, {self.rows})")
         flags = 0 if self._written_by_previous else FLAG_WEIGHTS_STABLE
         ctx = context(x.device.index)
-        st = _abi.load().ffai_int8_gemv(ctx, _ptr(x), batch, _ptr(self.qw), _ptr(self.bscale),
-                                        _ptr(self.corr), self.rows, self.cols, self.blk,
-                                        _ptr(out), flags, _stream(x.device))
+        st = _abi.load().ffai_int8_gemv(ctx, _ptr(x), batch, _ptr(self.packed), _ptr(self.corr),
+                                        self.rows, self.cols, self.blk, _ptr(out), flags,
+                                        _stream(x.device))
         _check(st, ctx)
         self._written_by_previous = False
         return out
 
-    def unpacked(self):
-        """(q (rows, cols) int8, scales (rows, cols / blk) f32, corr (rows,))."""
-        g = self.qw.numel() // (32 * self.cols)
-        nb = self.cols // self.blk
-        q = self.qw.view(g, self.cols // 16, 32, 16).permute(0, 2, 1, 3).reshape(g * 32, self.cols)
-        s = self.bscale.view(g, nb, 32).permute(0, 2, 1).reshape(g * 32, nb)
-        return q[:self.rows], s[:self.rows], self.corr[:self.rows]
+    def unpacked(self, padded: bool = False):
+        """(q (rows, cols) int8, scales (rows, cols / blk) f32, corr (rows,));
+        with `padded`, the zero rows up to the group boundary too."""
+        nb, blk = self.cols // self.blk, self.blk
+        g = self.corr.numel() // 32
+        recs = self.packed.view(g, nb, blk * 32 + 128)
+        w = recs[:, :, :blk * 32].reshape(g, nb, blk // 16, 32, 16)  # (g, b, c, l, j)
+        q = w.permute(0, 3, 1, 2, 4).reshape(g * 32, self.cols).view(torch.int8)
+        s = recs[:, :, blk * 32:].contiguous().view(torch.float32).view(g, nb, 32)
+        s = s.permute(0, 2, 1).reshape(g * 32, nb)
+        n = g * 32 if padded else self.rows
+        return q[:n], s[:n], self.corr[:n]

@@ -224,36 +224,38 @@ int ffai_kv_copy_pages(ffai_attn_ctx* ctx, const ffai_attn_desc* d, void* k_pool
  * shapes are FFAI_ATTN_DECLINED, as Int8Vocab::new (:102-131) returns None.
  *
  * The quantised weights are kept in a device layout of their own, rows padded
- * to G = ceil(rows / 32) groups of 32 (padding zero):
- *   qw     int8 (G, cols / 16, 32, 16): bytes [16c, 16c + 16) of row 32g + l
- *          at ((g * (cols / 16) + c) * 32 + l) * 16;
- *   bscale f32  (G, cols / blk, 32): scale of block b of row 32g + l at
- *          (g * (cols / blk) + b) * 32 + l;
- *   corr   f32  (G * 32).
- * Device buffers throughout. */
+ * to G = ceil(rows / 32) groups of 32 (padding zero).  Group g is cols / blk
+ * block records in column order (group g at byte g * (cols / blk) * R, R =
+ * blk * 32 + 128), record b holding, for the group's 32 rows l:
+ *   bytes [0, blk * 32): weight (int8) of column 16c + j of the block at
+ *          (c * 32 + l) * 16 + j;
+ *   bytes [blk * 32, R): the f32 scale of block b of row l at blk * 32 + 4 l.
+ * corr: f32 (G * 32).  Device buffers throughout. */
 
-/* Sizes of the three buffers for a (rows, cols) matrix: qw bytes, bscale and
- * corr element counts.  FFAI_ATTN_DECLINED for shapes not served. */
-int ffai_int8_gemv_layout(int32_t rows, int32_t cols, int32_t blk, int64_t* qw_bytes,
-                          int64_t* scale_count, int64_t* corr_count);
+/* Sizes of the two buffers for a (rows, cols) matrix: packed bytes and corr
+ * element count.  FFAI_ATTN_DECLINED for shapes not served. */
+int ffai_int8_gemv_layout(int32_t rows, int32_t cols, int32_t blk, int64_t* packed_bytes,
+                          int64_t* corr_count);
 
 /* Int8Vocab::new (vocab_int8.rs:97-166) on the device: W of w_dtype (f32,
  * bf16 or f16; widened to f32 exactly) into the layout above. */
 int ffai_int8_gemv_quantize(ffai_attn_ctx* ctx, const void* w, int32_t w_dtype, int32_t rows,
-                            int32_t cols, int32_t blk, int8_t* qw, float* bscale, float* corr,
-                            void* stream);
+                            int32_t cols, int32_t blk, void* packed, float* corr, void* stream);
 
 /* Int8VocabOp::cpu_fwd (vocab_int8.rs:218-305) for `batch` (1..8) activation
  * rows at once: x (batch, cols) f32 -> out (batch, rows) f32, each row
  * quantised on its own as the reference does per call; the weights are read
- * once for all rows.  qw and bscale 16-byte aligned.  flags: 0 or
+ * once for all rows (a small kernel quantises x into the context's scratch,
+ * then the GEMV kernel streams the weights: calls on one context must not
+ * run concurrently on different streams).  packed and x 16-byte aligned.
+ * flags: 0 or
  * FFAI_INT8_FLAG_WEIGHTS_STABLE -- the weights were not written by the kernel
  * launched just before on the stream, so the GEMV may start streaming them
  * before that kernel ends (x is always read after it). */
 #define FFAI_INT8_FLAG_WEIGHTS_STABLE 0x2u
-int ffai_int8_gemv(ffai_attn_ctx* ctx, const float* x, int32_t batch, const int8_t* qw,
-                   const float* bscale, const float* corr, int32_t rows, int32_t cols,
-                   int32_t blk, float* out, uint32_t flags, void* stream);
+int ffai_int8_gemv(ffai_attn_ctx* ctx, const float* x, int32_t batch, const void* packed,
+                   const float* corr, int32_t rows, int32_t cols, int32_t blk, float* out,
+                   uint32_t flags, void* stream);
 
 /* Variable-length (ragged) prefill over packed segments, TOKEN_MAJOR
  * (T, H, 64) operands and output.  Segment s owns query rows

@@ -28,6 +28,13 @@ namespace {
 
 float rust_round(float x) { return std::round(x); }  // half away from zero, like f32::round
 
+// f32::clamp then `as` to an integer: NaN (which clamp passes through)
+// becomes 0 under Rust's saturating cast.
+int rust_clamp_cast(float r, float lo, float hi) {
+  if (std::isnan(r)) return 0;
+  return static_cast<int>(std::fmin(std::fmax(r, lo), hi));
+}
+
 }  // namespace
 
 extern "C" {
@@ -50,9 +57,7 @@ int ora_int8_quantize(const float* w, int vocab, int d, int blk, int8_t* qw, flo
       bscale[static_cast<size_t>(v) * nb + b] = sc;
       int32_t bsum = 0;
       for (int k = 0; k < blk; ++k) {
-        float r = rust_round(bw[k] / sc);
-        r = std::fmin(std::fmax(r, -127.0f), 127.0f);
-        const int8_t qi = static_cast<int8_t>(r);
+        const int8_t qi = static_cast<int8_t>(rust_clamp_cast(rust_round(bw[k] / sc), -127.0f, 127.0f));
         qw[static_cast<size_t>(v) * d + b * blk + k] = qi;
         bsum += qi;
       }
@@ -75,9 +80,7 @@ void ora_int8_gemv(const float* x, int batch, const int8_t* qw, const float* bsc
     const float sx = amax > 0.f ? amax / 63.0f : 1.0f;
     std::vector<uint8_t> xu(d);
     for (int k = 0; k < d; ++k) {
-      float r = rust_round(xr[k] / sx);
-      r = std::fmin(std::fmax(r, -64.0f), 63.0f);
-      xu[k] = static_cast<uint8_t>(static_cast<int>(r) + 64);
+      xu[k] = static_cast<uint8_t>(rust_clamp_cast(rust_round(xr[k] / sx), -64.0f, 63.0f) + 64);
     }
     float* o = out + static_cast<size_t>(bi) * vocab;
     auto rows = [&](int v0, int v1) {

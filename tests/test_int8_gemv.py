@@ -21,8 +21,19 @@ def _round_half_away(x):
     return t + np.where(np.abs(x - t) >= np.float32(0.5), np.sign(x), np.float32(0)).astype(np.float32)
 
 
+def _clamp_cast(r, lo, hi):
+    """f32::clamp then Rust's saturating `as` cast: NaN -> 0."""
+    with np.errstate(invalid="ignore"):
+        return np.where(np.isnan(r), 0, np.clip(np.nan_to_num(r, nan=0.0), lo, hi)).astype(np.int64)
+
+
 def _scalar_reference(w, x, blk):
     """Int8Vocab::new + cpu_fwd + dot_i8_blocked with numpy f32 scalars."""
+    with np.errstate(all="ignore"):  # inf * 0 and inf / inf are part of the non-finite cases
+        return _scalar_reference_steps(w, x, blk)
+
+
+def _scalar_reference_steps(w, x, blk):
     f = np.float32
     vocab, d = w.shape
     nb = d // blk
@@ -34,17 +45,19 @@ def _scalar_reference(w, x, blk):
         c = f(0)
         for b in range(nb):
             bw = w[v, b * blk:(b + 1) * blk]
-            amax = f(np.max(np.abs(bw)))
+            amax = f(np.nanmax(np.concatenate([[0], np.abs(bw)])))
             sc = amax / f(127) if amax > 0 else f(1)
             bs[v, b] = sc
-            qb = np.clip(_round_half_away(bw / sc), -127, 127).astype(np.int64)
+            with np.errstate(invalid="ignore", divide="ignore"):
+                qb = _clamp_cast(_round_half_away(bw / sc), -127, 127)
             q[v, b * blk:(b + 1) * blk] = qb
             c = f(c + f(sc * f(int(qb.sum()))))
         corr[v] = f(64) * c
     for i, xr in enumerate(x):
-        amax = f(np.max(np.abs(xr)))
+        amax = f(np.nanmax(np.concatenate([[0], np.abs(xr)])))
         sx = amax / f(63) if amax > 0 else f(1)
-        xu = (np.clip(_round_half_away(xr / sx), -64, 63) + 64).astype(np.int64)
+        with np.errstate(invalid="ignore", divide="ignore"):
+            xu = _clamp_cast(_round_half_away(xr / sx), -64, 63) + 64
         for v in range(vocab):
             acc = f(0)
             for b in range(nb):
@@ -95,12 +108,43 @@ def test_oracle_matches_scalar_restatement(oracle, d, blk):
     assert np.array_equal(got.view(np.int32), out.view(np.int32))
 
 
+def _nonfinite_case(d, blk, seed):
+    rng = np.random.default_rng(seed)
+    w = rng.standard_normal((6, d), dtype=np.float32)
+    w[1, 3] = np.nan            # ignored by the block maximum, quantised to 0
+    w[2, blk + 1] = np.inf      # block scale inf: that row's output is not finite
+    w[4, 5] = -np.inf
+    x = rng.standard_normal((4, d), dtype=np.float32)
+    x[0, 7] = np.nan            # quantised to 0 (+ 64)
+    x[2, 1] = np.inf            # sx = inf
+    x[3, :] = np.float32(1e-30)  # tiny: sx far below the normal range of the fast path
+    x[3, 2] = np.float32(-2.5e-30)
+    return w, x
+
+
+def _same(a, b):
+    """Bit-equal, NaN equal to NaN (payloads are the platform's)."""
+    a, b = np.ascontiguousarray(a, np.float32), np.ascontiguousarray(b, np.float32)
+    na, nb_ = np.isnan(a), np.isnan(b)
+    return np.array_equal(na, nb_) and np.array_equal(a.view(np.int32)[~na], b.view(np.int32)[~nb_])
+
+
+@pytest.mark.parametrize("d,blk", [(96, 32), (192, 64)])
+def test_oracle_nonfinite_inputs(oracle, d, blk):
+    w, x = _nonfinite_case(d, blk, d)
+    q, bs, corr, out = _scalar_reference(w, x, blk)
+    qw, obs, ocorr = oracle.int8_quantize(w, blk)
+    assert np.array_equal(qw, q)
+    assert _same(obs, bs) and _same(ocorr, corr)
+    assert _same(oracle.int8_gemv(x, qw, obs, ocorr, blk, threads=1), out)
+
+
 def test_abi_layout():
     from ffai_b200.int8_gemv import layout
-    assert layout(51865, 1280, 32) == (51872 * 1280, 51872 * 40, 51872)
-    assert layout(384, 384, 96) == (384 * 384, 384 * 4, 384)
-    assert layout(1, 640, 640) == (32 * 640, 32, 32)
-    assert layout(100, 8192, 1024) == (128 * 8192, 128 * 8, 128)
+    assert layout(51865, 1280, 32) == (1621 * 40 * 1152, 51872)
+    assert layout(384, 384, 96) == (12 * 4 * (96 * 32 + 128), 384)
+    assert layout(1, 640, 640) == (640 * 32 + 128, 32)
+    assert layout(100, 8192, 1024) == (4 * 8 * (1024 * 32 + 128), 128)
     for rows, cols, blk in [(8, 20, 32), (8, 384, 48), (8, 384, 0), (8, 384, -32), (8, 0, 32),
                             (0, 384, 32), (8, 2048, 2048), (8, 8224, 32)]:
         assert layout(rows, cols, blk) is None, (rows, cols, blk)
@@ -137,6 +181,19 @@ def _bits_equal(a, b):
 
 
 @pytest.mark.gpu
+@pytest.mark.parametrize("d,blk", [(384, 32), (1280, 64)])
+def test_gemv_nonfinite_inputs(oracle, d, blk):
+    from ffai_b200.int8_gemv import Int8Gemv
+    w, x = _nonfinite_case(d, blk, d + 1)
+    q = Int8Gemv.new(torch.from_numpy(w).to(DEV), blk)
+    got = q.forward(torch.from_numpy(x).to(DEV)).cpu().numpy()
+    qw, bs, corr = oracle.int8_quantize(w, blk)
+    gq, gs, gc = (t.cpu().numpy() for t in q.unpacked())
+    assert np.array_equal(gq, qw) and _same(gs, bs) and _same(gc, corr)
+    assert _same(got, oracle.int8_gemv(x, qw, bs, corr, blk))
+
+
+@pytest.mark.gpu
 @pytest.mark.parametrize("rows,cols,blk,dtype", [
     (4096, 384, 32, torch.float32), (51865, 1280, 32, torch.float32),
     (5120, 1280, 64, torch.bfloat16), (1280, 5120, 32, torch.float16),
@@ -155,11 +212,9 @@ def test_quantize_matches_oracle(oracle, rows, cols, blk, dtype):
     assert _bits_equal(got_bs, bs)
     assert _bits_equal(got_corr, corr)
     # the padding rows of the last group are zero
-    g = q.qw.numel() // (32 * cols)
-    assert g * 32 - rows < 32
-    assert not q.corr[rows:].any()
-    full_q = q.qw.view(g, cols // 16, 32, 16).permute(0, 2, 1, 3).reshape(g * 32, cols)
-    assert not full_q[rows:].any()
+    pq, ps, pc = q.unpacked(padded=True)
+    assert pq.shape[0] - rows < 32
+    assert not pq[rows:].any() and not ps[rows:].any() and not pc[rows:].any()
 
 
 @pytest.mark.gpu
