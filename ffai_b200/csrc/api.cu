@@ -1384,7 +1384,7 @@ int ffai_int8_gemv_layout(int32_t rows, int32_t cols, int32_t blk, int64_t* pack
                      "(at most %d)", blk, kGvMaxBlk, cols, kGvMaxCols);
   const long long groups = int8_gemv_groups(rows);
   if (packed_bytes) *packed_bytes = groups * (cols / blk) * int8_gemv_record(blk);
-  if (corr_count) *corr_count = groups * 32;
+  if (corr_count) *corr_count = groups * kGvRows;
   return FFAI_ATTN_OK;
 }
 

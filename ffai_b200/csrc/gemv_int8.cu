@@ -16,23 +16,24 @@
 //     dot_i8_blocked, :280-305.
 //
 // B200 layout: the projection streams the whole weight matrix once per token
-// (75 MB for 51865 x 1280), so it is HBM-bound.  The integer block sums are
-// exact on the tensor cores (mma.sync m16n8k32, s8 weights x u8 activations
-// -> s32; the activation rows of a step -- beams, up to 8 -- are the 8
-// columns), which leaves the SIMT pipes the reference's f32 epilogue: per
-// block, convert and multiply by the row's scale (any warp), then add in
-// block order (one warp per 16 rows, in registers).
+// (75 MB for 51865 x 1280), so it is HBM-bound, and shared memory is the
+// next limit: every byte is written by the bulk copy and read once more.
+// The integer block sums are exact on the tensor cores (mma.sync m16n8k32,
+// s8 weights x u8 activations -> s32; the activation rows of a step -- beams,
+// up to 8 -- are the 8 columns), leaving the SIMT pipes the reference's f32
+// epilogue: per block, convert, multiply by the row's scale, add in block
+// order.  One warp owns a 16-row group (an m16 tile) for all its blocks, so
+// the ordered sum stays in its registers and nothing else touches shared
+// memory.
 //
 // Streaming: persistent CTAs, one per SM, each take a contiguous range of
-// 32-row groups, cut into units of S block records (weights and their scales
-// are contiguous in the packed layout, so a unit is ONE bulk copy).  Units
-// go through a ring of shared-memory slots, each refilled by its own
-// producer lane: bulk copies issued by one thread complete one after
-// another, so a ring only turns into bytes in flight when every slot has its
-// own issuing thread.  Fourteen compute warps share every unit (two m16
-// tiles x S blocks) and leave the f32 block products in the slot, over the
-// weights they came from; two summing warps add them in block order and
-// hand the slot back to its producer lane.
+// groups in rounds of one group per consumer warp.  A group is cut into units
+// of S block records (weights and their scales are contiguous in the packed
+// layout, so a unit is ONE bulk copy); a round's units go through a ring of
+// shared-memory slots unit-major (unit k of every group of the round, then
+// unit k + 1), each slot refilled by its own producer lane: bulk copies
+// issued by one thread complete one after another, so a ring only turns
+// into bytes in flight when every slot has its own issuing thread.
 #include <algorithm>
 #include <atomic>
 
@@ -43,19 +44,20 @@ namespace ffai {
 
 namespace {
 
-constexpr int kGvConsWarps = 16;
+#ifndef FFAI_GV_WARPS
+#define FFAI_GV_WARPS 24
+#endif
+constexpr int kGvConsWarps = FFAI_GV_WARPS;  // consumer warps: groups of a round
 constexpr int kGvThreads = (kGvConsWarps + 1) * 32;  // + the producer warp
 constexpr int kGvCons = kGvConsWarps * 32;
 #ifndef FFAI_GV_SLOT_TARGET
-#define FFAI_GV_SLOT_TARGET 24576
+#define FFAI_GV_SLOT_TARGET 6144
 #endif
 #ifndef FFAI_GV_RING_MAX
-#define FFAI_GV_RING_MAX 12
+#define FFAI_GV_RING_MAX 32
 #endif
 constexpr int kGvSlotTarget = FFAI_GV_SLOT_TARGET;  // bytes per slot to aim for
 constexpr int kGvMaxRing = FFAI_GV_RING_MAX;        // slots, one producer lane each
-constexpr int kGvComputeWarps = kGvConsWarps - 2;  // + two summing warps
-constexpr int kGvBlockStride = kGvComputeWarps / 2;  // blocks between a warp's blocks
 // Dynamic shared memory the kernel may use (227 KB per block, less a little
 // for its static arrays).
 constexpr int kGvSmemMax = 227 * 1024 - 1024;
@@ -73,13 +75,15 @@ __global__ void __launch_bounds__(256) int8_quantize_kernel(const T* w, int rows
                                                             uint8_t* packed, float* corr) {
   const int row = (blockIdx.x * blockDim.x + threadIdx.x) / 32;
   const int lane = threadIdx.x % 32;
-  const int padded = static_cast<int>(int8_gemv_groups(rows)) * 32;
+  const int padded = static_cast<int>(int8_gemv_groups(rows)) * kGvRows;
   if (row >= padded) return;
-  const int g = row / 32, l = row % 32, nb = cols / blk, rec = int8_gemv_record(blk);
+  const int g = row / kGvRows, l = row % kGvRows, nb = cols / blk, rec = int8_gemv_record(blk);
   auto record = [&](int b) { return packed + (static_cast<size_t>(g) * nb + b) * rec; };
   // column k (within block b) of this row
-  auto qbyte = [&](int b, int k) { return record(b) + ((k / 16) * 32 + l) * 16 + k % 16; };
-  auto scale = [&](int b) { return reinterpret_cast<float*>(record(b) + blk * 32) + l; };
+  auto qbyte = [&](int b, int k) { return record(b) + ((k / 16) * kGvRows + l) * 16 + k % 16; };
+  auto scale = [&](int b) {
+    return reinterpret_cast<float*>(record(b) + blk * kGvRows) + (l % 8) * 2 + l / 8;
+  };
   if (row >= rows) {
     for (int b = 0; b < nb; ++b) {
       for (int k = lane; k < blk; k += 32) *qbyte(b, k) = 0;
@@ -217,15 +221,39 @@ __global__ void __launch_bounds__(kActThreads) int8_act_kernel(const float* x, i
   }
 }
 
+// Wait (bounded, like mbar_wait) until the producer has armed use `use` of a
+// slot: from then on the slot's full barrier is in that use's phase, and a
+// parity wait on it is exact.
+__device__ __forceinline__ bool wait_slot_use(const int* use_armed, int use, volatile int* abort_flag,
+                                              unsigned* err) {
+  const volatile int* u = use_armed;
+  if (*u >= use) return true;
+  const unsigned long long t0 = globaltimer_ns();
+  while (*u < use) {
+    if (*abort_flag) return false;
+    if (globaltimer_ns() - t0 > kWaitLimitNs) {
+      *abort_flag = 1;
+      if (err) atomicOr(err, kErrTimeoutConsumer);
+      return false;
+    }
+    __nanosleep(64);
+  }
+  return true;
+}
+
 template <bool SMALL>
 __global__ void __launch_bounds__(kGvThreads, 1) int8_gemv_kernel(Int8GemvParams p) {
   const Int8GemvPlan& P = p.plan;
   extern __shared__ __align__(128) uint8_t dsm[];
   uint8_t* xq = dsm + P.x_off;
   uint64_t* full = reinterpret_cast<uint64_t*>(dsm + P.bar_off);
-  uint64_t* ready = full + kGvMaxRing;   // compute warps wrote the slot's products
-  uint64_t* empty = ready + kGvMaxRing;  // summing warps read them
+  uint64_t* empty = full + kGvMaxRing;
   __shared__ float s_sx[kGvMaxBatch];
+  // s_use[r]: the use of slot r the producer has armed last.  Warps consume
+  // different units and may run ahead of one another, so a warp can come to
+  // wait for use m of a slot while use m - 1 is still in flight; a parity
+  // wait cannot tell those apart, the counter can.
+  __shared__ int s_use[kGvMaxRing];
   __shared__ int s_abort;
 
   const int tid = threadIdx.x, warp = tid / 32, lane = tid % 32;
@@ -235,13 +263,12 @@ __global__ void __launch_bounds__(kGvThreads, 1) int8_gemv_kernel(Int8GemvParams
   const int upg = (nb + S - 1) / S;  // units (slot loads) per group
   const int g_begin = static_cast<int>(static_cast<long long>(blockIdx.x) * P.groups / P.grid);
   const int g_end = static_cast<int>(static_cast<long long>(blockIdx.x + 1) * P.groups / P.grid);
-  const int units = (g_end - g_begin) * upg;
 
   if (tid == 0) {
     for (int i = 0; i < ring; ++i) {
       mbar_init(&full[i], 1);
-      mbar_init(&ready[i], kGvComputeWarps);
-      mbar_init(&empty[i], 2);
+      mbar_init(&empty[i], 1);  // the warp that owns the unit's group
+      s_use[i] = -1;
     }
     s_abort = 0;
     fence_mbar_init();
@@ -249,29 +276,36 @@ __global__ void __launch_bounds__(kGvThreads, 1) int8_gemv_kernel(Int8GemvParams
   __syncthreads();
   griddep_launch_dependents();
 
-  // Producer: lane r refills slot r with units r, r + ring, ... (unit u =
-  // group u / upg of the CTA, blocks [k S, k S + S) with k = u % upg), each
-  // ONE bulk copy.  Stable weights stream while the preceding kernel
+  // Producer: units in stream order j (round by round: unit k of each of
+  // the round's groups, k = 0 .. upg - 1); lane r refills slot r with units
+  // r, r + ring, ...  Stable weights stream while the preceding kernel
   // finishes; the activations come from it, so the consumers always wait.
   if (warp == kGvConsWarps) {
     if (!p.weights_stable) griddep_wait();
     if (lane >= ring) return;
     uint64_t* fb = &full[lane];
+    const int units = (g_end - g_begin) * upg;
+    const int full_round = kGvConsWarps * upg;  // units of a full round
     int issued = 0;
     bool ok = true;
-    for (int u = lane; u < units; u += ring) {
+    for (int j = lane; j < units; j += ring, ++issued) {
       if (issued > 0 &&
           !mbar_wait(&empty[lane], (issued - 1) & 1, &s_abort, p.err, kErrTimeoutProducer)) {
         ok = false;
         break;
       }
-      const int k = u % upg;
-      const size_t g = static_cast<size_t>(g_begin + u / upg);
+      const int ro = j / full_round, g0 = g_begin + ro * kGvConsWarps;
+      const int n = min(kGvConsWarps, g_end - g0), rem = j - ro * full_round;
+      const int k = rem / n, i = rem - k * n;
       const uint32_t bytes = static_cast<uint32_t>(min(S, nb - k * S)) * rec;
+      // The uses before this one have landed and been consumed (empty above).
+      // A plain store: shared memory has one copy, and a fence here would
+      // wait for this warp's earlier bulk copies.
+      *reinterpret_cast<volatile int*>(&s_use[lane]) = issued;
       mbar_arrive_expect_tx(fb, bytes);
       bulk_load(dsm + static_cast<size_t>(lane) * P.slot_bytes,
-                p.packed + (g * nb + static_cast<size_t>(k) * S) * rec, bytes, fb);
-      ++issued;
+                p.packed + (static_cast<size_t>(g0 + i) * nb + static_cast<size_t>(k) * S) * rec,
+                bytes, fb);
     }
     if (issued > 0 && (!ok || s_abort)) {
       // Let this slot's last copy land before the CTA exits.
@@ -293,107 +327,88 @@ __global__ void __launch_bounds__(kGvThreads, 1) int8_gemv_kernel(Int8GemvParams
   }
   named_bar_sync(kGvBarX, kGvCons);
 
-  // Consumers.  Compute warps c = 0 .. 13 take m16 tile c & 1 (rows
-  // 16 (c & 1) ..) of blocks c / 2, c / 2 + 7, ... of every unit and write
-  // the f32 block products over the weights they have just read (16 rows x
-  // 16 bytes of the block's first two chunks: 512 bytes, one float4 a lane).
-  // Warps 14 and 15 add a unit's products in block order for tile 0 / 1,
-  // keeping a group's sums in registers, and release the slot.
+  // Consumers: warp w takes group w of each round, all its blocks in order;
+  // thread (gq, tig) accumulates rows gq, gq + 8 x beams 2 tig, 2 tig + 1.
   const int gq = lane >> 2, tig = lane & 3;
-  if (warp < kGvComputeWarps) {
-    const int mt = warp & 1, kb0 = warp >> 1;
-    // ldmatrix row addresses: A -- lanes 8j..8j+7 give rows of matrix j
-    // (j = 0, 1: chunk 2s, rows 0-7 / 8-15; j = 2, 3: chunk 2s + 1);
-    // B -- lanes 0-7 / 8-15 give the 8 activation rows of chunk 2s / 2s + 1.
-    const uint32_t a_lane = (((lane >> 4) * 32) + (lane & 7) + ((lane >> 3) & 1) * 8 + 16 * mt) * 16;
-    const uint32_t b_lane = ((((lane >> 3) & 1) * 8) + (lane & 7)) * 16;
-    const uint32_t prod_lane = (lane >> 4) * 512 + mt * 256 + (lane & 15) * 16;
-    const uint32_t xq_s = smem_u32(xq), dsm_s = smem_u32(dsm);
-    for (int u = 0; u < units; ++u) {
-      const int k = u % upg, r = u % ring;
-      if (!mbar_wait(&full[r], (u / ring) & 1, &s_abort, p.err, kErrTimeoutConsumer)) break;
+  // ldmatrix row addresses: A -- lanes 8m .. 8m + 7 give the rows of matrix m
+  // (m = 0, 1: chunk 2s, rows 0-7 / 8-15; m = 2, 3: chunk 2s + 1);
+  // B -- lanes 0-7 / 8-15 give the 8 activation rows of chunk 2s / 2s + 1.
+  const uint32_t a_lane = ((lane >> 4) * kGvRows + (lane & 7) + ((lane >> 3) & 1) * 8) * 16;
+  const uint32_t b_lane = ((((lane >> 3) & 1) * 8) + (lane & 7)) * 16;
+  const uint32_t xq_s = smem_u32(xq), dsm_s = smem_u32(dsm);
+  int j0 = 0;  // stream index of the round's first unit
+  for (int g0 = g_begin; g0 < g_end; g0 += kGvConsWarps) {
+    const int n = min(kGvConsWarps, g_end - g0);
+    if (warp >= n) {
+      j0 += n * upg;
+      continue;
+    }
+    float acc[4] = {0.f, 0.f, 0.f, 0.f};
+    bool ok = true;
+    for (int k = 0; k < upg; ++k) {
+      const int j = j0 + k * n + warp, r = j % ring, use = j / ring;
+      if (!wait_slot_use(&s_use[r], use, &s_abort, p.err) ||
+          !mbar_wait(&full[r], use & 1, &s_abort, p.err, kErrTimeoutConsumer)) {
+        ok = false;
+        break;
+      }
       const int sk = min(S, nb - k * S);
       const uint32_t slot_s = dsm_s + r * P.slot_bytes;
-      for (int kbb = kb0; kbb < sk; kbb += kGvBlockStride * kGvBatch) {
+      // kGvBatch blocks at a time: their loads and mmas all in flight before
+      // the products are added in block order
+      for (int kb0 = 0; kb0 < sk; kb0 += kGvBatch) {
         int d[kGvBatch][4];
         uint32_t rec_s[kGvBatch], x_s[kGvBatch];
 #pragma unroll
         for (int i = 0; i < kGvBatch; ++i) {
-          // past the end: a valid block, result unused
-          const int kb = min(kbb + kGvBlockStride * i, sk - 1);
+          const int kb = min(kb0 + i, sk - 1);  // past the end: a valid block, result unused
           rec_s[i] = slot_s + kb * rec;
           x_s[i] = xq_s + static_cast<uint32_t>((k * S + kb) * gc) * 128;
 #pragma unroll
-          for (int j = 0; j < 4; ++j) d[i][j] = 0;
+          for (int t = 0; t < 4; ++t) d[i][t] = 0;
         }
         for (int sl = 0; sl < gc / 2; ++sl) {
           uint32_t a[kGvBatch][4], bx[kGvBatch][2];
 #pragma unroll
           for (int i = 0; i < kGvBatch; ++i) {
-            ldsm_x4(rec_s[i] + sl * 1024 + a_lane, a[i][0], a[i][1], a[i][2], a[i][3]);
+            ldsm_x4(rec_s[i] + sl * 512 + a_lane, a[i][0], a[i][1], a[i][2], a[i][3]);
             ldsm_x2(x_s[i] + sl * 256 + b_lane, bx[i][0], bx[i][1]);
           }
 #pragma unroll
           for (int i = 0; i < kGvBatch; ++i)
             mma_s8u8(d[i], a[i][0], a[i][1], a[i][2], a[i][3], bx[i][0], bx[i][1]);
         }
+        float2 sc[kGvBatch];
+#pragma unroll
+        for (int i = 0; i < kGvBatch; ++i)
+          sc[i] = *reinterpret_cast<const float2*>(dsm + (rec_s[i] - dsm_s) + blk * kGvRows + gq * 8);
 #pragma unroll
         for (int i = 0; i < kGvBatch; ++i) {
-          if (kbb + kGvBlockStride * i < sk) {
-            uint8_t* recp = dsm + (rec_s[i] - dsm_s);
-            const float* sc = reinterpret_cast<const float*>(recp + blk * 32) + 16 * mt + gq;
-            const float s0 = sc[0], s1 = sc[8];
-            *reinterpret_cast<float4*>(recp + prod_lane) =
-                make_float4(__fmul_rn(sum_to_f32<SMALL>(d[i][0]), s0),
-                            __fmul_rn(sum_to_f32<SMALL>(d[i][1]), s0),
-                            __fmul_rn(sum_to_f32<SMALL>(d[i][2]), s1),
-                            __fmul_rn(sum_to_f32<SMALL>(d[i][3]), s1));
+          if (kb0 + i < sk) {
+            acc[0] = __fadd_rn(acc[0], __fmul_rn(sum_to_f32<SMALL>(d[i][0]), sc[i].x));
+            acc[1] = __fadd_rn(acc[1], __fmul_rn(sum_to_f32<SMALL>(d[i][1]), sc[i].x));
+            acc[2] = __fadd_rn(acc[2], __fmul_rn(sum_to_f32<SMALL>(d[i][2]), sc[i].y));
+            acc[3] = __fadd_rn(acc[3], __fmul_rn(sum_to_f32<SMALL>(d[i][3]), sc[i].y));
           }
         }
       }
-      fence_proxy_async_smem();  // the slot is refilled by a bulk copy after the summers read it
       __syncwarp();
-      if (lane == 0) mbar_arrive(&ready[r]);
+      if (lane == 0) mbar_arrive(&empty[r]);
     }
-    return;
-  }
-
-  // Summing warps: tile st of every unit, the products in block order.
-  const int st = warp - kGvComputeWarps;
-  const uint32_t prod_lane = (lane >> 4) * 512 + st * 256 + (lane & 15) * 16;
-  float acc[4] = {0.f, 0.f, 0.f, 0.f};
-  for (int u = 0; u < units; ++u) {
-    const int li = u / upg, k = u - li * upg, r = u % ring;
-    if (!mbar_wait(&ready[r], (u / ring) & 1, &s_abort, p.err, kErrTimeoutConsumer)) break;
-    const int sk = min(S, nb - k * S);
-    const uint8_t* src = dsm + static_cast<size_t>(r) * P.slot_bytes + prod_lane;
-    for (int kb = 0; kb < sk; ++kb) {
-      const float4 v = *reinterpret_cast<const float4*>(src + kb * rec);
-      acc[0] = __fadd_rn(acc[0], v.x);
-      acc[1] = __fadd_rn(acc[1], v.y);
-      acc[2] = __fadd_rn(acc[2], v.z);
-      acc[3] = __fadd_rn(acc[3], v.w);
-    }
-    fence_proxy_async_smem();
-    __syncwarp();
-    if (lane == 0) mbar_arrive(&empty[r]);
-    if (k == upg - 1) {
-      // thread (gq, tig) holds rows gq, gq + 8 of tile st, beams 2 tig, 2 tig + 1
-      const int r0 = (g_begin + li) * 32 + 16 * st + gq, r1 = r0 + 8;
+    j0 += n * upg;
+    if (!ok) break;
+    const int r0 = (g0 + warp) * kGvRows + gq, r1 = r0 + 8;
 #pragma unroll
-      for (int e = 0; e < 2; ++e) {
-        const int b = 2 * tig + e;
-        if (b >= B) continue;
-        const float sx = s_sx[b];
-        if (r0 < p.rows)
-          p.out[static_cast<size_t>(b) * p.rows + r0] =
-              __fmul_rn(__fsub_rn(acc[e], __ldg(p.corr + r0)), sx);
-        if (r1 < p.rows)
-          p.out[static_cast<size_t>(b) * p.rows + r1] =
-              __fmul_rn(__fsub_rn(acc[2 + e], __ldg(p.corr + r1)), sx);
-      }
-#pragma unroll
-      for (int j = 0; j < 4; ++j) acc[j] = 0.f;
+    for (int e = 0; e < 2; ++e) {
+      const int b = 2 * tig + e;
+      if (b >= B) continue;
+      const float sx = s_sx[b];
+      if (r0 < p.rows)
+        p.out[static_cast<size_t>(b) * p.rows + r0] =
+            __fmul_rn(__fsub_rn(acc[e], __ldg(p.corr + r0)), sx);
+      if (r1 < p.rows)
+        p.out[static_cast<size_t>(b) * p.rows + r1] =
+            __fmul_rn(__fsub_rn(acc[2 + e], __ldg(p.corr + r1)), sx);
     }
   }
 }
@@ -412,7 +427,7 @@ bool int8_gemv_plan(int rows, int cols, int blk, int batch, int sms, Int8GemvPla
   P.S = (nb + upg - 1) / upg;
   P.slot_bytes = P.S * rec;
   const int x_bytes = (cols / 16) * 128;
-  const int bar_bytes = 3 * kGvMaxRing * 8;
+  const int bar_bytes = 2 * kGvMaxRing * 8;
   const int avail = kGvSmemMax - x_bytes - bar_bytes;
   P.ring = std::min(kGvMaxRing, avail / P.slot_bytes);
   if (P.ring < 2) return false;

@@ -76,29 +76,35 @@ cudaError_t launch_kv_copy_pages(const DecodeParams& p, const int* src, const in
 
 // ---- int8 GEMV (gemv_int8.cu) ----------------------------------------------
 
-// Device layout of the quantised weights: rows padded to G = ceil(rows / 32)
-// groups of 32 (padding zero); group g is nb = cols / blk block records in
-// column order, each kGvRecord(blk) = blk * 32 + 128 bytes:
-//   bytes [0, blk * 32): chunk c (16 columns) of the block for row l at
-//     (c * 32 + l) * 16 -- 32 rows x 16 bytes per chunk, so 8 rows of a chunk
+// Device layout of the quantised weights: rows padded to G = ceil(rows / 16)
+// groups of 16 (padding zero); group g is nb = cols / blk block records in
+// column order, each int8_gemv_record(blk) = blk * 16 + 64 bytes:
+//   bytes [0, blk * 16): chunk c (16 columns) of the block for row l at
+//     (c * 16 + l) * 16 -- 16 rows x 16 bytes per chunk, so 8 rows of a chunk
 //     are one 128-byte matrix for ldmatrix;
-//   bytes [blk * 32, blk * 32 + 128): the 32 rows' f32 block scales.
+//   bytes [blk * 16, blk * 16 + 64): the 16 rows' f32 block scales, row l at
+//     float (l % 8) * 2 + l / 8 (rows l and l + 8 side by side, as the mma's
+//     accumulator fragment holds them).
 // A group's records are contiguous (group g at g * nb * record bytes), so
-// any run of a group's blocks is one bulk copy.  corr: (G * 32) f32.
+// any run of a group's blocks is one bulk copy.  corr: (G * 16) f32.
 constexpr int kGvMaxBatch = 8;
 constexpr int kGvMaxCols = 8192;
 constexpr int kGvMaxBlk = 1024;
+constexpr int kGvRows = 16;  // rows per group
 
-__host__ __device__ inline int int8_gemv_record(int blk) { return blk * 32 + 128; }
+__host__ __device__ inline int int8_gemv_record(int blk) { return blk * kGvRows + 64; }
 inline bool int8_gemv_served(int cols, int blk) {
   return blk > 0 && blk % 32 == 0 && blk <= kGvMaxBlk && cols > 0 && cols % blk == 0 &&
          cols <= kGvMaxCols;
 }
-__host__ __device__ inline long long int8_gemv_groups(long long rows) { return (rows + 31) / 32; }
+__host__ __device__ inline long long int8_gemv_groups(long long rows) {
+  return (rows + kGvRows - 1) / kGvRows;
+}
 
 // Launch geometry, computed on the host.  CTA c takes the contiguous groups
-// [c * groups / grid, (c + 1) * groups / grid), streamed as units of S block
-// records of one group through a ring of `ring` shared-memory slots.
+// [c * groups / grid, (c + 1) * groups / grid) in rounds of one group per
+// consumer warp, each group cut into units of S block records streamed
+// through a ring of `ring` shared-memory slots, unit-major within a round.
 struct Int8GemvPlan {
   int groups, grid, ring, S;
   int slot_bytes;  // S * record bytes

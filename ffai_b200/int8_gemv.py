@@ -8,7 +8,7 @@ None for a shape it does not serve (as `Int8Vocab::new` does);
 `forward(x)` maps (batch, cols) f32 activations (batch <= 8, e.g. the beams
 of a step) to (batch, rows) f32 in one pass over the weights.  The quantised
 weights live in the library's device layout of block records (weights and
-scales of 32 rows x one block together); `unpacked()` returns them as the
+scales of 16 rows x one block together); `unpacked()` returns them as the
 reference holds them (row-major q, (rows, nblocks) scales, corr).
 """
 
@@ -95,12 +95,14 @@ class Int8Gemv:
     def unpacked(self, padded: bool = False):
         """(q (rows, cols) int8, scales (rows, cols / blk) f32, corr (rows,));
         with `padded`, the zero rows up to the group boundary too."""
-        nb, blk = self.cols // self.blk, self.blk
-        g = self.corr.numel() // 32
-        recs = self.packed.view(g, nb, blk * 32 + 128)
-        w = recs[:, :, :blk * 32].reshape(g, nb, blk // 16, 32, 16)  # (g, b, c, l, j)
-        q = w.permute(0, 3, 1, 2, 4).reshape(g * 32, self.cols).view(torch.int8)
-        s = recs[:, :, blk * 32:].contiguous().view(torch.float32).view(g, nb, 32)
-        s = s.permute(0, 2, 1).reshape(g * 32, nb)
-        n = g * 32 if padded else self.rows
+        nb, blk, R = self.cols // self.blk, self.blk, 16
+        g = self.corr.numel() // R
+        recs = self.packed.view(g, nb, blk * R + 64)
+        w = recs[:, :, :blk * R].reshape(g, nb, blk // 16, R, 16)  # (g, b, c, l, j)
+        q = w.permute(0, 3, 1, 2, 4).reshape(g * R, self.cols).view(torch.int8)
+        s = recs[:, :, blk * R:].contiguous().view(torch.float32).view(g, nb, R)
+        # row l's scale sits at (l % 8) * 2 + l // 8
+        perm = torch.tensor([(l % 8) * 2 + l // 8 for l in range(R)], device=s.device)
+        s = s[:, :, perm].permute(0, 2, 1).reshape(g * R, nb)
+        n = g * R if padded else self.rows
         return q[:n], s[:n], self.corr[:n]
