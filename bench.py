@@ -432,6 +432,86 @@ def bench_int8_gemv(steps: int, dev):
     return res
 
 
+def bench_f16_gemv(steps: int, dev):
+    """The decoder's f16 GEMVs (the reference's F16Gemv, its default for the
+    single-row projections) on large-v3's shapes for 1 and 5 activation rows:
+    the self-attention q/k/v stacked into one 3840 x 1280 call, the 1280 x 1280
+    out-projection, fc1 (5120 x 1280) and fc2 (1280 x 5120), each over 32
+    layers' distinct weights in a CUDA graph; and a 51865 x 1280 matrix (a
+    vocabulary-sized projection) for the kernel's streaming rate."""
+    import torch
+
+    from ffai_b200.f16_gemv import F16Gemv
+    from oracle import oracle
+    res = {}
+    g = torch.Generator(device=dev).manual_seed(13)
+
+    def graph_time(calls, reps):
+        for c in calls:
+            c()
+        torch.cuda.synchronize()
+        gr = torch.cuda.CUDAGraph()
+        s = torch.cuda.Stream()
+        s.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(s):
+            for c in calls:
+                c()
+            torch.cuda.synchronize()
+            with torch.cuda.graph(gr, stream=s):
+                for c in calls:
+                    c()
+        torch.cuda.current_stream().wait_stream(s)
+        for _ in range(3):
+            gr.replay()
+        torch.cuda.synchronize()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        for _ in range(reps):
+            gr.replay()
+        b.record()
+        torch.cuda.synchronize()
+        del gr
+        return a.elapsed_time(b) / 1e3 / (reps * len(calls))
+
+    layer = (("qkv_3840x1280", 3840, 1280), ("o_1280x1280", 1280, 1280),
+             ("fc1_5120x1280", 5120, 1280), ("fc2_1280x5120", 1280, 5120))
+    for name, rows, cols, copies in [(n, r, c, 32) for n, r, c in layer] + [
+            ("vocab_51865x1280", 51865, 1280, 2)]:
+        qs = [F16Gemv.new(torch.randn(rows, cols, device=dev, generator=g) * 0.05,
+                          torch.randn(rows, device=dev, generator=g)) for _ in range(copies)]
+        for batch in (1, 5):
+            x = torch.randn(batch, cols, device=dev, generator=g)
+            outs = [torch.empty(batch, rows, device=dev) for _ in qs]
+            t = graph_time([lambda q=q, o=o: q.forward(x, out=o) for q, o in zip(qs, outs)],
+                           max(2, steps // 4))
+            nbytes = rows * cols * 2 + 4 * rows + batch * 4 * (cols + rows)
+            res[f"{name}_b{batch}"] = {"kernel": "f16_gemv_kernel", "bytes_per_launch": nbytes,
+                                      "us_per_launch": round(t * 1e6, 2),
+                                      "gbs": round(nbytes / t / 1e9, 1)}
+        del qs
+    per_layer = sum(res[f"{n}_b5"]["us_per_launch"] for n, _, _ in layer)
+    res["decoder_layer_projections_b5_us"] = round(per_layer, 2)
+    # the reference's CPU GEMV (oracle restatement, all host threads), 1 row, fc1
+    import numpy as np
+    oracle.build()
+    rng = np.random.default_rng(4)
+    w16 = oracle.f16_weights(rng.standard_normal((5120, 1280), dtype=np.float32) * np.float32(0.05))
+    xn = rng.standard_normal((1, 1280), dtype=np.float32)
+    threads = os.cpu_count() or 1
+    oracle.f16_gemv(xn, w16, threads=threads)
+    runs, t0 = 0, time.perf_counter()
+    while time.perf_counter() - t0 < 1.0 or runs == 0:
+        oracle.f16_gemv(xn, w16, threads=threads)
+        runs += 1
+    tc = (time.perf_counter() - t0) / runs
+    nbytes = 5120 * 1280 * 2 + 4 * (1280 + 5120)
+    res["cpu_fc1_5120x1280_b1"] = {
+        "kind": "port", "cores": threads, "us_per_call": round(tc * 1e6, 1),
+        "gbs": round(nbytes / tc / 1e9, 2),
+        "sample": f"{runs} call(s) of the oracle's f16_gemv.rs restatement, 1 activation row"}
+    return res
+
+
 def bench_ragged(dist, steps: int, peaks):
     """c5: 256 packed segments of U{200..1500} frames, 16 heads, through the
     varlen entry; segments assigned to ranks longest-processing-time first on
@@ -612,6 +692,13 @@ def run_ours(args, dist):
         for v_ in decode.values():
             v_["frac_of_hbm"] = round(v_["gbs_graph"] / peaks["hbm_gbs"], 4)
 
+    f16 = None
+    if dist.rank == 0 and not args.no_f16:
+        f16 = bench_f16_gemv(max(5, min(args.steps, 50)), torch.device("cuda", torch.cuda.current_device()))
+        for k_, v_ in f16.items():
+            if isinstance(v_, dict) and not k_.startswith("cpu"):
+                v_["frac_of_hbm"] = round(v_["gbs"] / peaks["hbm_gbs"], 4)
+
     int8 = None
     if dist.rank == 0 and not args.no_int8:
         int8 = bench_int8_gemv(max(5, min(args.steps, 50)), torch.device("cuda", torch.cuda.current_device()))
@@ -657,6 +744,7 @@ def run_ours(args, dist):
             "decode": decode,
             "ragged_c5": ragged,
             "int8_gemv": int8,
+            "f16_gemv": f16,
         }
         print(json.dumps(line), flush=True)
     dist.barrier()
@@ -673,6 +761,7 @@ def main():
     ap.add_argument("--no-decode", action="store_true")
     ap.add_argument("--no-ragged", action="store_true")
     ap.add_argument("--no-int8", action="store_true")
+    ap.add_argument("--no-f16", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--segments", type=int, default=0,

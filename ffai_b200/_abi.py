@@ -89,6 +89,10 @@ SIGNATURES = {
     "ffai_kv_append": ([_vp, _DescP, _vp, _vp, _i32, _vp, _vp, _i32, _vp, _vp, _vp], ctypes.c_int),
     "ffai_kv_copy_pages": ([_vp, _DescP, _vp, _vp, _i32, _vp, _vp, _i32, _vp], ctypes.c_int),
     "ffai_int8_gemv_layout": ([_i32, _i32, _i32, _vp, _vp], ctypes.c_int),
+    "ffai_f16_gemv_layout": ([_i32, _i32, _vp], ctypes.c_int),
+    "ffai_f16_gemv_pack": ([_vp, _vp, _i32, _i32, _i32, _vp, _vp], ctypes.c_int),
+    "ffai_f16_gemv": ([_vp, _vp, _i32, _vp, _vp, _i32, _i32, _vp, ctypes.c_uint32, _vp],
+                      ctypes.c_int),
     "ffai_int8_gemv_quantize": ([_vp, _vp, _i32, _i32, _i32, _i32, _vp, _vp, _vp], ctypes.c_int),
     "ffai_int8_gemv": ([_vp, _vp, _i32, _vp, _vp, _i32, _i32, _i32, _vp, ctypes.c_uint32, _vp],
                        ctypes.c_int),

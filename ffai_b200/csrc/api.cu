@@ -1446,4 +1446,67 @@ int ffai_int8_gemv(ffai_attn_ctx* ctx, const float* x, int32_t batch, const void
   return FFAI_ATTN_OK;
 }
 
+
+// ---------------------------------------------------------------------------
+// f16 GEMV (the reference's F16Gemv, f16_gemv.rs)
+
+int ffai_f16_gemv_layout(int32_t rows, int32_t cols, int64_t* packed_bytes) {
+  if (rows <= 0 || !f16_gemv_served(cols))
+    return set_error(nullptr, FFAI_ATTN_DECLINED,
+                     "f16 GEMV: cols %d must be a positive multiple of 8 (at most %d)", cols,
+                     kHgMaxCols);
+  if (packed_bytes)
+    *packed_bytes = f16_gemv_groups(rows) * f16_gemv_steps(cols) * kHgRows * 16 * 2;
+  return FFAI_ATTN_OK;
+}
+
+int ffai_f16_gemv_pack(ffai_attn_ctx* ctx, const void* w, int32_t w_dtype, int32_t rows,
+                       int32_t cols, void* packed, void* stream) {
+  if (!ctx) return set_error(nullptr, FFAI_ATTN_ERR_INVALID, "null context");
+  if (rows <= 0 || !f16_gemv_served(cols))
+    return set_error(ctx, FFAI_ATTN_DECLINED,
+                     "f16 GEMV: cols %d must be a positive multiple of 8 (at most %d)", cols,
+                     kHgMaxCols);
+  if (!valid_dtype(w_dtype)) return set_error(ctx, FFAI_ATTN_ERR_INVALID, "unknown weight dtype");
+  if (!w || !packed) return set_error(ctx, FFAI_ATTN_ERR_INVALID, "f16 GEMV pack: null pointer");
+  DeviceGuard g(ctx->device);
+  FFAI_CUDA(ctx, launch_f16_pack(w, w_dtype, rows, cols, static_cast<uint16_t*>(packed),
+                                 static_cast<cudaStream_t>(stream)));
+  return FFAI_ATTN_OK;
+}
+
+int ffai_f16_gemv(ffai_attn_ctx* ctx, const float* x, int32_t batch, const void* packed,
+                  const float* bias, int32_t rows, int32_t cols, float* out, uint32_t flags,
+                  void* stream) {
+  if (!ctx) return set_error(nullptr, FFAI_ATTN_ERR_INVALID, "null context");
+  if (flags & ~FFAI_GEMV_FLAG_WEIGHTS_STABLE)
+    return set_error(ctx, FFAI_ATTN_ERR_INVALID, "f16 GEMV: unknown flags 0x%x", flags);
+  if (rows <= 0 || !f16_gemv_served(cols))
+    return set_error(ctx, FFAI_ATTN_DECLINED,
+                     "f16 GEMV: cols %d must be a positive multiple of 8 (at most %d)", cols,
+                     kHgMaxCols);
+  if (batch < 1 || batch > kHgMaxBatch)
+    return set_error(ctx, FFAI_ATTN_ERR_INVALID, "f16 GEMV: batch %d not in [1, %d]", batch,
+                     kHgMaxBatch);
+  if (!x || !packed || !out) return set_error(ctx, FFAI_ATTN_ERR_INVALID, "f16 GEMV: null pointer");
+  if (reinterpret_cast<uintptr_t>(packed) % 16 != 0)
+    return set_error(ctx, FFAI_ATTN_ERR_INVALID, "f16 GEMV: packed weights 16-byte aligned");
+  F16GemvParams p{};
+  if (!f16_gemv_plan(rows, cols, batch, ctx->num_sms, &p.plan))
+    return set_error(ctx, FFAI_ATTN_DECLINED, "f16 GEMV: no shared-memory plan for %d x %d", rows,
+                     cols);
+  DeviceGuard g(ctx->device);
+  p.x = x;
+  p.batch = batch;
+  p.packed = static_cast<const uint16_t*>(packed);
+  p.bias = bias;
+  p.rows = rows;
+  p.cols = cols;
+  p.out = out;
+  p.err = ctx->d_err;
+  p.weights_stable = (flags & FFAI_GEMV_FLAG_WEIGHTS_STABLE) != 0;
+  FFAI_CUDA(ctx, launch_f16_gemv(p, static_cast<cudaStream_t>(stream)));
+  return FFAI_ATTN_OK;
+}
+
 }  // extern "C"

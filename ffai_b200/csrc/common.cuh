@@ -103,6 +103,28 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
   }
 }
 
+// Rings whose consumers take different units (and so may run ahead of one
+// another): the producer records in use_armed the use of a slot it armed last,
+// and a consumer waits (bounded, like mbar_wait) until its use is armed; from
+// then on the slot's full barrier is in that use's phase, and a parity wait on
+// it is exact.
+__device__ __forceinline__ bool wait_slot_use(const int* use_armed, int use, volatile int* abort_flag,
+                                              unsigned* err) {
+  const volatile int* u = use_armed;
+  if (*u >= use) return true;
+  const unsigned long long t0 = globaltimer_ns();
+  while (*u < use) {
+    if (*abort_flag) return false;
+    if (globaltimer_ns() - t0 > kWaitLimitNs) {
+      *abort_flag = 1;
+      if (err) atomicOr(err, kErrTimeoutConsumer);
+      return false;
+    }
+    __nanosleep(64);
+  }
+  return true;
+}
+
 // ------------------------------------------- programmatic dependent launch
 
 // Let a grid launched after this one as a programmatic dependent start

@@ -221,26 +221,6 @@ __global__ void __launch_bounds__(kActThreads) int8_act_kernel(const float* x, i
   }
 }
 
-// Wait (bounded, like mbar_wait) until the producer has armed use `use` of a
-// slot: from then on the slot's full barrier is in that use's phase, and a
-// parity wait on it is exact.
-__device__ __forceinline__ bool wait_slot_use(const int* use_armed, int use, volatile int* abort_flag,
-                                              unsigned* err) {
-  const volatile int* u = use_armed;
-  if (*u >= use) return true;
-  const unsigned long long t0 = globaltimer_ns();
-  while (*u < use) {
-    if (*abort_flag) return false;
-    if (globaltimer_ns() - t0 > kWaitLimitNs) {
-      *abort_flag = 1;
-      if (err) atomicOr(err, kErrTimeoutConsumer);
-      return false;
-    }
-    __nanosleep(64);
-  }
-  return true;
-}
-
 template <bool SMALL>
 __global__ void __launch_bounds__(kGvThreads, 1) int8_gemv_kernel(Int8GemvParams p) {
   const Int8GemvPlan& P = p.plan;

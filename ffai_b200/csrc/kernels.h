@@ -130,6 +130,53 @@ cudaError_t launch_int8_quantize(const void* w, int w_dtype, int rows, int cols,
                                  uint8_t* packed, float* corr, cudaStream_t s);
 cudaError_t launch_int8_gemv(const Int8GemvParams& p, cudaStream_t s);
 
+// ---- f16 GEMV (gemv_f16.cu) ------------------------------------------------
+
+// Device layout of the f16 weights: rows padded to groups of kHgRows = 8
+// (padding zero); group g is steps j = 0 .. ceil(cols / 16) - 1 of 256 bytes:
+// for each of the 16 columns 16 j + c, the group's rows 4 s + i (s = 0, 1;
+// i = 0 .. 3) at halfword ((g * steps + j) * 16 + c) * 8 + 4 s + i -- so lane
+// (s, c) of a warp reads its 4 rows' weights of a column as one 8-byte load
+// and the warp's step is 256 contiguous bytes.  Columns past `cols` (cols %
+// 16 == 8) are zero and never read.  A group's steps are contiguous, so a
+// run of them is one bulk copy.
+constexpr int kHgRows = 8;
+constexpr int kHgLaneRows = 4;  // rows per lane
+constexpr int kHgMaxBatch = 8;
+constexpr int kHgMaxCols = 65536;
+
+__host__ __device__ inline long long f16_gemv_groups(long long rows) {
+  return (rows + kHgRows - 1) / kHgRows;
+}
+__host__ __device__ inline int f16_gemv_steps(int cols) { return (cols + 15) / 16; }
+inline bool f16_gemv_served(int cols) { return cols > 0 && cols % 8 == 0 && cols <= kHgMaxCols; }
+
+// Launch geometry (host): as for the int8 GEMV -- CTA c takes a contiguous
+// range of groups in rounds of one group per consumer warp, each group cut
+// into units of S steps streamed unit-major through `ring` slots.
+struct F16GemvPlan {
+  int groups, grid, ring, S;
+  int slot_bytes;  // S * 64
+  int bar_off, x_off, x_pitch, smem;  // x_pitch 0: activations read through L1
+};
+bool f16_gemv_plan(int rows, int cols, int batch, int sms, F16GemvPlan* plan);
+
+struct F16GemvParams {
+  const float* x;           // (batch, cols) f32 activations
+  int batch;                // 1..8
+  const uint16_t* packed;   // f16 weights (layout above)
+  const float* bias;        // (rows) or null
+  int rows, cols;           // f16_gemv_served(cols)
+  float* out;               // (batch, rows)
+  unsigned* err;
+  int weights_stable;       // weights not written by the preceding kernel
+  F16GemvPlan plan;
+};
+
+cudaError_t launch_f16_pack(const void* w, int w_dtype, int rows, int cols, uint16_t* packed,
+                            cudaStream_t s);
+cudaError_t launch_f16_gemv(const F16GemvParams& p, cudaStream_t s);
+
 // ---- checked f32 prefill (prefill_simt.cu) ---------------------------------
 
 // Element offset of (b, h, row, d) is b*sb + h*sh + row*sr + d*sd.

@@ -253,9 +253,41 @@ int ffai_int8_gemv_quantize(ffai_attn_ctx* ctx, const void* w, int32_t w_dtype, 
  * launched just before on the stream, so the GEMV may start streaming them
  * before that kernel ends (x is always read after it). */
 #define FFAI_INT8_FLAG_WEIGHTS_STABLE 0x2u
+#define FFAI_GEMV_FLAG_WEIGHTS_STABLE 0x2u /* the same flag, for ffai_f16_gemv */
 int ffai_int8_gemv(ffai_attn_ctx* ctx, const float* x, int32_t batch, const void* packed,
                    const float* corr, int32_t rows, int32_t cols, int32_t blk, float* out,
                    uint32_t flags, void* stream);
+
+/* ---- f16 GEMV ----------------------------------------------------------
+ * The reference's F16Gemv (f16_gemv.rs), the default path of the decoder's
+ * single-row projections (QLinear::Half, text_decoder.rs:106-118, :231-252):
+ * weights rounded to f16 once, f32 fused multiply-adds in 16 chains of
+ * columns (chain c: columns 16 j + c in order of j; an 8-column tail feeds
+ * chains 0-7), reduced as ((a0 + a4) + (a2 + a6)) + ((a1 + a5) + (a3 + a7))
+ * with a_i = c_i + c_{i+8}; outputs equal the reference's bit for bit (NaN
+ * payloads aside).  cols a positive multiple of 8 (f16_gemv.rs:99-103),
+ * at most 65536.  Device layout of the f16 weights: rows in groups of 8;
+ * group g is ceil(cols / 16) steps of 16 columns x 8 rows (256 bytes):
+ * column 16 j + c of row 8 g + i at halfword ((g * steps + j) * 16 + c) * 8
+ * + i, padding zero. */
+
+/* Bytes of the packed f16 weights; FFAI_ATTN_DECLINED when not served. */
+int ffai_f16_gemv_layout(int32_t rows, int32_t cols, int64_t* packed_bytes);
+
+/* F16Gemv::new (f16_gemv.rs:89-119) on the device: W (rows, cols) row-major
+ * of w_dtype, rounded to f16 (nearest-even) into the layout above. */
+int ffai_f16_gemv_pack(ffai_attn_ctx* ctx, const void* w, int32_t w_dtype, int32_t rows,
+                       int32_t cols, void* packed, void* stream);
+
+/* F16GemvOp::cpu_fwd (f16_gemv.rs:145-164) for `batch` (1..8) activation
+ * rows at once (the reference loops rows, text_decoder.rs:158-170): x
+ * (batch, cols) f32 -> out (batch, rows) f32, plus bias (rows) when not
+ * null, added after the dot product as QLinear::forward does (:281-289).
+ * packed 16-byte aligned; flags 0 or FFAI_GEMV_FLAG_WEIGHTS_STABLE (the
+ * weights were not written by the kernel launched just before). */
+int ffai_f16_gemv(ffai_attn_ctx* ctx, const float* x, int32_t batch, const void* packed,
+                  const float* bias, int32_t rows, int32_t cols, float* out, uint32_t flags,
+                  void* stream);
 
 /* Variable-length (ragged) prefill over packed segments, TOKEN_MAJOR
  * (T, H, 64) operands and output.  Segment s owns query rows

@@ -63,6 +63,9 @@ def lib():
             "ora_three_op": ([_f32p, _f32p, _f32p, _f32p, i, i, i], None),
             "ora_int8_quantize": ([_f32p, i, i, i, ctypes.c_void_p, _f32p, _f32p], i),
             "ora_int8_gemv": ([_f32p, i, ctypes.c_void_p, _f32p, _f32p, i, i, i, _f32p, i], None),
+            "ora_f16_round": ([_f32p, ctypes.c_longlong, ctypes.c_void_p], None),
+            "ora_f16_serves": ([i], i),
+            "ora_f16_gemv": ([_f32p, i, ctypes.c_void_p, _f32p, i, i, _f32p, i], None),
         }
         for name, (args, res) in sig.items():
             fn = getattr(L, name)
@@ -287,5 +290,32 @@ def int8_gemv(x, qw, bscale, corr, blk=32, threads=None):
     out = np.empty((x.shape[0], vocab), np.float32)
     lib().ora_int8_gemv(_p(x), x.shape[0], qw.ctypes.data_as(ctypes.c_void_p), _p(_f32(bscale)),
                         _p(_f32(corr)), vocab, d, blk, _p(out), threads or default_threads())
+    return out
+
+
+# --------------------------------------------------------------------------
+# f16 GEMV (f16_gemv.rs), restated in f16_gemv_ref.cpp
+# --------------------------------------------------------------------------
+
+def f16_weights(w):
+    """F16Gemv::new's weights: f32 -> f16 bits (nearest-even), same shape, uint16;
+    None when the shape is not served (cols not a multiple of 8)."""
+    w = _f32(w)
+    if w.ndim != 2 or lib().ora_f16_serves(w.shape[1]) != 0:
+        return None
+    out = np.empty(w.shape, np.uint16)
+    lib().ora_f16_round(_p(w), w.size, out.ctypes.data_as(ctypes.c_void_p))
+    return out
+
+
+def f16_gemv(x, w16, bias=None, threads=None):
+    """dot_f16 per activation row (+ bias after): x (batch, cols) -> (batch, rows)."""
+    x = _f32(np.atleast_2d(x))
+    w16 = np.ascontiguousarray(w16, np.uint16)
+    rows, cols = w16.shape
+    out = np.empty((x.shape[0], rows), np.float32)
+    b = None if bias is None else _f32(bias)
+    lib().ora_f16_gemv(_p(x), x.shape[0], w16.ctypes.data_as(ctypes.c_void_p),
+                       None if b is None else _p(b), rows, cols, _p(out), threads or default_threads())
     return out
 
