@@ -90,6 +90,8 @@ SIGNATURES = {
     "ffai_kv_copy_pages": ([_vp, _DescP, _vp, _vp, _i32, _vp, _vp, _i32, _vp], ctypes.c_int),
     "ffai_int8_gemv_layout": ([_i32, _i32, _i32, _vp, _vp], ctypes.c_int),
     "ffai_f16_gemv_layout": ([_i32, _i32, _vp], ctypes.c_int),
+    "ffai_gemm_bf16": ([_vp, _vp, ctypes.c_int64, _vp, ctypes.c_int64, _vp, _vp, ctypes.c_int64,
+                        _vp, ctypes.c_int64, _i32, _i32, _i32, _i32, _i32, _vp], ctypes.c_int),
     "ffai_f16_gemv_pack": ([_vp, _vp, _i32, _i32, _i32, _vp, _vp], ctypes.c_int),
     "ffai_f16_gemv": ([_vp, _vp, _i32, _vp, _vp, _i32, _i32, _vp, ctypes.c_uint32, _vp],
                       ctypes.c_int),

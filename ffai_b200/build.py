@@ -17,7 +17,7 @@ INCLUDE = os.path.join(os.path.dirname(PKG_DIR), "include")
 LIB_PATH = os.path.join(PKG_DIR, "libffai_attn.so")
 
 SOURCES = ["api.cu", "decode.cu", "prefill_simt.cu", "prefill_tc.cu", "convert.cu",
-           "gemv_int8.cu", "gemv_f16.cu"]
+           "gemv_int8.cu", "gemv_f16.cu", "gemm_tc.cu"]
 NVCC_FLAGS = [
     "-gencode", "arch=compute_100a,code=sm_100a",
     "-O3", "-lineinfo", "-std=c++17",

@@ -1510,3 +1510,82 @@ int ffai_f16_gemv(ffai_attn_ctx* ctx, const float* x, int32_t batch, const void*
 }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------------------
+// bf16 GEMM with a fused epilogue (the projections around the attention)
+
+namespace {
+
+// 2-d tensor map over a row-major (rows, cols) matrix with row stride ld
+// elements: box box_cols x box_rows; the box's rows (box_cols x element
+// size bytes) swizzled at that width (128 or 64 bytes).
+int make_map_2d(ffai_attn_ctx* ctx, CUtensorMap* map, const void* base, long long cols,
+                long long rows, long long ld, int box_rows, bool f32 = false, int box_cols = 64) {
+  if (!g_encode) return set_error(ctx, FFAI_ATTN_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
+  const int esize = f32 ? 4 : 2;
+  const cuuint64_t dims[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows)};
+  const cuuint64_t strides[1] = {static_cast<cuuint64_t>(ld) * esize};
+  const cuuint32_t box[2] = {static_cast<cuuint32_t>(box_cols), static_cast<cuuint32_t>(box_rows)};
+  const cuuint32_t estr[2] = {1, 1};
+  const CUtensorMapSwizzle sw =
+      box_cols * esize == 128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B;
+  const CUresult r = g_encode(map, f32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16,
+                              2, const_cast<void*>(base), dims, strides, box, estr,
+                              CU_TENSOR_MAP_INTERLEAVE_NONE, sw, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return set_error(ctx, FFAI_ATTN_ERR_CUDA, "cuTensorMapEncodeTiled: %d", r);
+  return FFAI_ATTN_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int ffai_gemm_bf16(ffai_attn_ctx* ctx, const void* a, int64_t lda, const void* b, int64_t ldb,
+                   const float* bias, const void* residual, int64_t ldr, void* out, int64_t ldo,
+                   int32_t M, int32_t N, int32_t K, int32_t out_dtype, int32_t act, void* stream) {
+  if (!ctx) return set_error(nullptr, FFAI_ATTN_ERR_INVALID, "null context");
+  if (M <= 0 || N <= 0 || K <= 0)
+    return set_error(ctx, FFAI_ATTN_ERR_INVALID, "GEMM: empty shape %d x %d x %d", M, N, K);
+  if (N % 32 != 0 || K % 8 != 0)
+    return set_error(ctx, FFAI_ATTN_DECLINED, "GEMM: N (%d) a multiple of 32, K (%d) of 8", N, K);
+  if (out_dtype != FFAI_DT_F32 && out_dtype != FFAI_DT_BF16)
+    return set_error(ctx, FFAI_ATTN_ERR_INVALID, "GEMM: output f32 or bf16");
+  if (act != FFAI_GEMM_ACT_NONE && act != FFAI_GEMM_ACT_FAST_GELU)
+    return set_error(ctx, FFAI_ATTN_ERR_INVALID, "GEMM: unknown activation %d", act);
+  if (!a || !b || !out) return set_error(ctx, FFAI_ATTN_ERR_INVALID, "GEMM: null pointer");
+  const int vec = out_dtype == FFAI_DT_F32 ? 4 : 8;  // elements per 16-byte access
+  if (lda < K || ldb < K || lda % 8 != 0 || ldb % 8 != 0 || ldo < N || ldo % vec != 0 ||
+      (residual && (ldr < N || ldr % vec != 0)))
+    return set_error(ctx, FFAI_ATTN_ERR_INVALID, "GEMM: leading dimensions (16-byte rows)");
+  for (const void* q : {a, b, static_cast<const void*>(out), residual, static_cast<const void*>(bias)})
+    if (q && reinterpret_cast<uintptr_t>(q) % 16 != 0)
+      return set_error(ctx, FFAI_ATTN_ERR_INVALID, "GEMM: operands 16-byte aligned");
+  DeviceGuard g(ctx->device);
+  CUtensorMap tma, tmb;
+  int st = make_map_2d(ctx, &tma, a, K, M, lda, 128);
+  if (st) return st;
+  st = make_map_2d(ctx, &tmb, b, K, N, ldb, 256);
+  if (st) return st;
+  CUtensorMap tmo;  // 32 x 32 output blocks for the epilogue's TMA stores
+  st = make_map_2d(ctx, &tmo, out, N, M, ldo, 32, out_dtype == FFAI_DT_F32, 32);
+  if (st) return st;
+  GemmParams p{};
+  p.M = M;
+  p.N = N;
+  p.K = K;
+  p.m_tiles = (M + 127) / 128;
+  p.n_tiles = (N + 255) / 256;
+  p.bias = bias;
+  p.residual = residual;
+  p.ldr = ldr;
+  p.out = out;
+  p.ldo = ldo;
+  p.out_f32 = out_dtype == FFAI_DT_F32;
+  p.act = act;
+  p.err = ctx->d_err;
+  FFAI_CUDA(ctx, launch_gemm(tma, tmb, tmo, p, ctx->num_sms, static_cast<cudaStream_t>(stream)));
+  return FFAI_ATTN_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,347 @@
+// bf16 GEMM on the tensor cores with a fused epilogue, for the projections
+// around the attention: out = act(A . B^T + bias) (+ residual).
+//
+// The reference runs these on candle's CPU GEMM (f32): the encoder's fc1 ->
+// GELU -> fc2 with the residual add (audio_encoder.rs:147-165), the q/k/v
+// projection whose head split feeds the attention (text_decoder.rs:1083-1124)
+// and the out-projection.  Here A (M x K, activations) and B (N x K, weights
+// as stored: (out, in)) are bf16, accumulation f32 in tensor memory, and the
+// epilogue adds the bias, applies the reference's FastGelu (gelu_scalar,
+// text_decoder.rs:341-350, same f32 operations in the same order) and the
+// residual, and stores bf16 or f32.
+//
+// B200 structure: persistent CTAs, one per SM, over 128 x 256 output tiles
+// (all n-tiles of an m-tile adjacent, so the activation tile stays in L2).
+// Warp 8 is the TMA producer (4-stage ring of 128 x 64 A and 256 x 64 B
+// tiles, 128-byte swizzle), warp 9 issues tcgen05.mma (M = 128, N = 256,
+// K = 16 steps) into one of two TMEM accumulators, so the epilogue of a tile
+// overlaps the main loop of the next; warps 0-7 are the epilogue (warp w
+// reads TMEM lanes 32 (w % 4) .., columns 128 (w / 4) ..).  Every wait is
+// bounded; on a time-out the CTA drains its copies and MMAs, frees TMEM and
+// leaves an error bit.
+#include <atomic>
+
+#include "common.cuh"
+#include "kernels.h"
+
+namespace ffai {
+
+namespace {
+
+constexpr int kGmBM = 128, kGmBN = 256, kGmBK = 64;
+constexpr int kGmStages = 4;
+constexpr int kGmABytes = kGmBM * kGmBK * 2;   // 16 KB
+constexpr int kGmBBytes = kGmBN * kGmBK * 2;   // 32 KB
+constexpr int kGmStageBytes = kGmABytes + kGmBBytes;
+constexpr int kGmEpiWarps = 8;
+constexpr int kGmEpiCols = kGmBN / (kGmEpiWarps / 4);  // columns per epilogue warp
+// Per epilogue warp, the staging of its 32 x 32 output blocks for the TMA
+// store: one f32 block or two bf16 blocks (double-buffered).
+constexpr int kGmStageOut = 4096;
+constexpr int kGmProducer = kGmEpiWarps, kGmMma = kGmEpiWarps + 1;
+constexpr int kGmThreads = (kGmEpiWarps + 2) * 32;
+constexpr int kGmTmemCols = 2 * kGmBN;  // two accumulators
+
+struct GmBars {
+  uint64_t full[kGmStages], empty[kGmStages];
+  uint64_t acc_full[2], acc_empty[2];
+  uint64_t done;
+  uint32_t tmem_base;
+  int abort_flag;
+};
+constexpr size_t kGmSmem =
+    1024 + kGmStages * kGmStageBytes + kGmEpiWarps * kGmStageOut + sizeof(GmBars) + 64;
+
+// Whisper's GELU as the reference computes it (gelu_scalar): a Pade 7/8
+// tanh, every operation a separately rounded f32 multiply or add.
+__device__ __forceinline__ float fast_gelu(float t) {
+  const float u = __fmul_rn(0.7978846f, __fmaf_rn(__fmul_rn(__fmul_rn(0.044715f, t), t), t, t));
+  const float u2 = fminf(__fmul_rn(u, u), 64.0f);
+  const float num = __fmul_rn(
+      u, __fadd_rn(135135.0f,
+                   __fmul_rn(u2, __fadd_rn(17325.0f, __fmul_rn(u2, __fadd_rn(378.0f, u2))))));
+  const float den = __fadd_rn(
+      135135.0f,
+      __fmul_rn(u2, __fadd_rn(62370.0f, __fmul_rn(u2, __fadd_rn(3150.0f, __fmul_rn(u2, 28.0f))))));
+  const float r = fminf(fmaxf(__fdiv_rn(num, den), -1.0f), 1.0f);
+  return __fmul_rn(__fmul_rn(0.5f, t), __fadd_rn(1.0f, r));
+}
+
+__device__ __forceinline__ void tma_load_2d(void* smem_dst, const CUtensorMap* map, uint64_t* bar,
+                                            int c0, int c1) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%2, %3}], [%4];" ::"r"(smem_u32(smem_dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(smem_u32(bar))
+      : "memory");
+}
+
+__device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, const void* smem_src, int c0,
+                                             int c1) {
+  asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];" ::"l"(
+                   reinterpret_cast<uint64_t>(map)),
+               "r"(smem_u32(smem_src)), "r"(c0), "r"(c1)
+               : "memory");
+}
+__device__ __forceinline__ void bulk_wait_read_1() {
+  asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory");
+}
+
+__global__ void __launch_bounds__(kGmThreads, 1)
+    gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                   const __grid_constant__ CUtensorMap tmO, GemmParams p) {
+  extern __shared__ uint8_t dsm_raw[];
+  // 1024-byte alignment for the 128-byte swizzle atoms
+  uint8_t* dsm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(dsm_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* stage_out = dsm + kGmStages * kGmStageBytes;
+  GmBars* bars = reinterpret_cast<GmBars*>(stage_out + kGmEpiWarps * kGmStageOut);
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  const int tiles = p.m_tiles * p.n_tiles;
+  const int kblocks = (p.K + kGmBK - 1) / kGmBK;
+  volatile int* abort_flag = &bars->abort_flag;
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < kGmStages; ++i) {
+      mbar_init(&bars->full[i], 1);
+      mbar_init(&bars->empty[i], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&bars->acc_full[i], 1);
+      mbar_init(&bars->acc_empty[i], kGmEpiWarps);
+    }
+    mbar_init(&bars->done, 1);
+    bars->abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == kGmMma) {
+    tmem_alloc(&bars->tmem_base, kGmTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = bars->tmem_base;
+  griddep_launch_dependents();
+
+  if (warp == kGmProducer) {
+    if (lane == 0) {
+      griddep_wait();  // A may come from the preceding kernel
+      prefetch_tensormap(&tmA);
+      prefetch_tensormap(&tmB);
+      uint32_t it = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < tiles && ok; t += gridDim.x) {
+        const int tm = t / p.n_tiles, tn = t - tm * p.n_tiles;
+        for (int kb = 0; kb < kblocks; ++kb, ++it) {
+          const uint32_t s = it % kGmStages;
+          if (it >= kGmStages &&
+              !mbar_wait(&bars->empty[s], ((it / kGmStages) - 1) & 1, abort_flag, p.err,
+                         kErrTimeoutProducer)) {
+            ok = false;
+            break;
+          }
+          uint8_t* sa = dsm + s * kGmStageBytes;
+          mbar_arrive_expect_tx(&bars->full[s], kGmStageBytes);
+          tma_load_2d(sa, &tmA, &bars->full[s], kb * kGmBK, tm * kGmBM);
+          tma_load_2d(sa + kGmABytes, &tmB, &bars->full[s], kb * kGmBK, tn * kGmBN);
+        }
+      }
+      if (!ok || *abort_flag) {
+        // let the copies in flight land before the CTA exits
+        int none = 0;
+        for (uint32_t i = 0; i < kGmStages && i < it; ++i) {
+          const uint32_t arms = (it - 1 - i) / kGmStages + 1;
+          mbar_wait(&bars->full[i], (arms - 1) & 1, &none, p.err, kErrTimeoutDrain);
+        }
+      }
+    }
+  } else if (warp == kGmMma) {
+    if (lane == 0) {
+      constexpr uint32_t idesc = idesc_f16(1u, kGmBM, kGmBN, 0, 0);
+      uint32_t it = 0, ti = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < tiles && ok; t += gridDim.x, ++ti) {
+        const uint32_t acc = ti & 1;
+        if (ti >= 2 && !mbar_wait(&bars->acc_empty[acc], ((ti >> 1) - 1) & 1, abort_flag, p.err,
+                                  kErrTimeoutMma)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        for (int kb = 0; kb < kblocks; ++kb, ++it) {
+          const uint32_t s = it % kGmStages;
+          if (!mbar_wait(&bars->full[s], (it / kGmStages) & 1, abort_flag, p.err, kErrTimeoutMma)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint64_t da = smem_desc_sw128(smem_u32(dsm + s * kGmStageBytes), 16, 1024);
+          const uint64_t db = smem_desc_sw128(smem_u32(dsm + s * kGmStageBytes + kGmABytes), 16, 1024);
+#pragma unroll
+          for (int k = 0; k < kGmBK / 16; ++k)  // +32 bytes per K step inside the swizzle atom
+            mma_ss(tmem + acc * kGmBN, da + 2 * k, db + 2 * k, idesc, (kb > 0 || k > 0) ? 1u : 0u);
+          mma_commit(&bars->empty[s]);
+        }
+        if (!ok) break;
+        mma_commit(&bars->acc_full[acc]);
+      }
+      // every MMA issued has finished before TMEM is freed
+      mma_commit(&bars->done);
+      int none = 0;
+      mbar_wait(&bars->done, 0, &none, p.err, kErrTimeoutDrain);
+    }
+  } else {
+    // Epilogue: warp w, TMEM lanes 32 (w % 4) + i = tile row, columns
+    // kGmEpiCols (w / 4) + [0, kGmEpiCols).  Each 32 x 32 block goes through
+    // a swizzled shared-memory staging buffer to one TMA store (rows past M
+    // are clipped by the store).  The residual and the output may belong to
+    // the preceding kernel.
+    griddep_wait();
+    const int lg = warp & 3, ch = warp >> 2;
+    uint8_t* stg = stage_out + warp * kGmStageOut;
+    uint32_t stores = 0;
+    uint32_t ti = 0;
+    for (int t = blockIdx.x; t < tiles; t += gridDim.x, ++ti) {
+      const uint32_t acc = ti & 1;
+      if (!mbar_wait(&bars->acc_full[acc], (ti >> 1) & 1, abort_flag, p.err, kErrTimeoutConsumer))
+        break;
+      tc_fence_after();
+      const int tm = t / p.n_tiles, tn = t - tm * p.n_tiles;
+      const int row0 = tm * kGmBM + 32 * lg;
+      const long long row = static_cast<long long>(row0) + lane;
+      for (int c0 = 0; c0 < kGmEpiCols; c0 += 32) {
+        uint32_t r[32];
+        tmem_ld32(tmem + acc * kGmBN + (static_cast<uint32_t>(32 * lg) << 16) + kGmEpiCols * ch + c0, r);
+        tmem_wait_ld();
+        const int n0 = tn * kGmBN + kGmEpiCols * ch + c0;
+        if (n0 >= p.N) continue;  // warp-uniform; N % 32 == 0
+        float v[32];
+#pragma unroll
+        for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+        if (p.bias != nullptr) {
+          // the same 32 values for every lane: 8 broadcast 16-byte loads
+          const float4* b4 = reinterpret_cast<const float4*>(p.bias + n0);
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            const float4 bb = __ldg(b4 + i);
+            v[4 * i] = __fadd_rn(v[4 * i], bb.x);
+            v[4 * i + 1] = __fadd_rn(v[4 * i + 1], bb.y);
+            v[4 * i + 2] = __fadd_rn(v[4 * i + 2], bb.z);
+            v[4 * i + 3] = __fadd_rn(v[4 * i + 3], bb.w);
+          }
+        }
+        if (p.act == 1) {
+#pragma unroll
+          for (int i = 0; i < 32; ++i) v[i] = fast_gelu(v[i]);
+        }
+        const bool has_row = row < p.M;
+        if (p.out_f32) {
+          if (p.residual != nullptr && has_row) {
+            const float* res = static_cast<const float*>(p.residual) + row * p.ldr + n0;
+#pragma unroll
+            for (int i = 0; i < 32; i += 4) {
+              const float4 q = *reinterpret_cast<const float4*>(res + i);
+              v[i] = __fadd_rn(v[i], q.x);
+              v[i + 1] = __fadd_rn(v[i + 1], q.y);
+              v[i + 2] = __fadd_rn(v[i + 2], q.z);
+              v[i + 3] = __fadd_rn(v[i + 3], q.w);
+            }
+          }
+          // 128-byte rows, 128-byte swizzle: 16-byte unit k of row r at k ^ (r % 8)
+          if (lane == 0) bulk_wait_read_all();
+          __syncwarp();
+#pragma unroll
+          for (int k = 0; k < 8; ++k)
+            *reinterpret_cast<float4*>(stg + lane * 128 + ((k ^ (lane & 7)) << 4)) =
+                make_float4(v[4 * k], v[4 * k + 1], v[4 * k + 2], v[4 * k + 3]);
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) {
+            tma_store_2d(&tmO, stg, n0, row0);
+            bulk_commit();
+          }
+        } else {
+          if (p.residual != nullptr && has_row) {
+            const uint16_t* res = static_cast<const uint16_t*>(p.residual) + row * p.ldr + n0;
+#pragma unroll
+            for (int i = 0; i < 32; i += 8) {
+              const uint4 q = *reinterpret_cast<const uint4*>(res + i);
+              const uint32_t qq[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+              for (int e = 0; e < 4; ++e) {
+                v[i + 2 * e] = __fadd_rn(v[i + 2 * e], lo_half(qq[e], 0));
+                v[i + 2 * e + 1] = __fadd_rn(v[i + 2 * e + 1], hi_half(qq[e], 0));
+              }
+            }
+          }
+          // two buffers; 64-byte rows, 64-byte swizzle: unit k of row r at k ^ ((r / 2) % 4)
+          uint8_t* buf = stg + (stores & 1) * 2048;
+          if (lane == 0) bulk_wait_read_1();  // the store that used this buffer has read it
+          __syncwarp();
+#pragma unroll
+          for (int k = 0; k < 4; ++k) {
+            uint4 pk;
+            pk.x = pack_bf16x2(v[8 * k], v[8 * k + 1]);
+            pk.y = pack_bf16x2(v[8 * k + 2], v[8 * k + 3]);
+            pk.z = pack_bf16x2(v[8 * k + 4], v[8 * k + 5]);
+            pk.w = pack_bf16x2(v[8 * k + 6], v[8 * k + 7]);
+            *reinterpret_cast<uint4*>(buf + lane * 64 + ((k ^ ((lane >> 1) & 3)) << 4)) = pk;
+          }
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) {
+            tma_store_2d(&tmO, buf, n0, row0);
+            bulk_commit();
+          }
+        }
+        ++stores;
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&bars->acc_empty[acc]);
+    }
+    if (lane == 0) bulk_wait_all();  // the output is written before the CTA ends
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == kGmMma) {
+    tc_fence_after();
+    tmem_dealloc(tmem, kGmTmemCols);
+  }
+}
+
+}  // namespace
+
+size_t gemm_smem_bytes() { return kGmSmem; }
+
+cudaError_t launch_gemm(const CUtensorMap& tmA, const CUtensorMap& tmB, const CUtensorMap& tmO,
+                        const GemmParams& p, int sms, cudaStream_t s) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  static std::atomic<bool> configured[64];
+  if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+  if (!configured[dev].load(std::memory_order_acquire)) {
+    e = cudaFuncSetAttribute(gemm_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             static_cast<int>(kGmSmem));
+    if (e != cudaSuccess) return e;
+    configured[dev].store(true, std::memory_order_release);
+  }
+  const int tiles = p.m_tiles * p.n_tiles;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3(static_cast<unsigned>(tiles < sms ? tiles : sms));
+  cfg.blockDim = dim3(kGmThreads);
+  cfg.dynamicSmemBytes = kGmSmem;
+  cfg.stream = s;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  e = cudaLaunchKernelEx(&cfg, gemm_tc_kernel, tmA, tmB, tmO, p);
+  if (e != cudaSuccess) return e;
+  return cudaGetLastError();
+}
+
+}  // namespace ffai

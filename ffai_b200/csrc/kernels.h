@@ -177,6 +177,27 @@ cudaError_t launch_f16_pack(const void* w, int w_dtype, int rows, int cols, uint
                             cudaStream_t s);
 cudaError_t launch_f16_gemv(const F16GemvParams& p, cudaStream_t s);
 
+// ---- bf16 GEMM with a fused epilogue (gemm_tc.cu) ---------------------------
+
+// out[m][n] = act(sum_k A[m][k] B[n][k] + bias[n]) (+ residual[m][n]);
+// A, B bf16 row-major (B as weights are stored, (N, K)); act 0 none, 1 the
+// reference's FastGelu; out / residual bf16 or f32 (out_f32).
+struct GemmParams {
+  int M, N, K;
+  int m_tiles, n_tiles;
+  const float* bias;       // (N) or null
+  const void* residual;    // (M, ldr) of the output type, or null
+  long long ldr;
+  void* out;               // (M, ldo)
+  long long ldo;
+  int out_f32;
+  int act;
+  unsigned* err;
+};
+size_t gemm_smem_bytes();
+cudaError_t launch_gemm(const CUtensorMap& tmA, const CUtensorMap& tmB, const CUtensorMap& tmO,
+                        const GemmParams& p, int sms, cudaStream_t s);
+
 // ---- checked f32 prefill (prefill_simt.cu) ---------------------------------
 
 // Element offset of (b, h, row, d) is b*sb + h*sh + row*sr + d*sd.

@@ -289,6 +289,26 @@ int ffai_f16_gemv(ffai_attn_ctx* ctx, const float* x, int32_t batch, const void*
                   const float* bias, int32_t rows, int32_t cols, float* out, uint32_t flags,
                   void* stream);
 
+/* ---- bf16 GEMM with a fused epilogue ------------------------------------
+ * The projections around the attention, which the reference runs on candle's
+ * CPU GEMM: the encoder MLP (fc1 -> FastGelu -> fc2 + residual,
+ * audio_encoder.rs:147-165), the q/k/v projection that feeds the attention in
+ * its layout (text_decoder.rs:1083-1124) and the out-projection:
+ *   out[m][n] = act(sum_k a[m][k] b[n][k] + bias[n]) (+ residual[m][n])
+ * a (M, K) and b (N, K) bf16 row-major (b as weights are stored), leading
+ * dimensions in elements (multiples of 8); bias f32 (N) or null; out and
+ * residual of out_dtype (FFAI_DT_F32 or FFAI_DT_BF16), residual null for
+ * none; act FFAI_GEMM_ACT_FAST_GELU applies the reference's FastGelu
+ * (text_decoder.rs:341-350) in f32 before the residual.  N a multiple of 32,
+ * K of 8 (else FFAI_ATTN_DECLINED); f32 accumulation on the tensor cores.
+ * The q/k/v projection's output (T, 3 * H * 64) is the attention's three
+ * TOKEN_MAJOR operands with token_stride = 3 * H * 64, as it stands. */
+#define FFAI_GEMM_ACT_NONE 0
+#define FFAI_GEMM_ACT_FAST_GELU 1
+int ffai_gemm_bf16(ffai_attn_ctx* ctx, const void* a, int64_t lda, const void* b, int64_t ldb,
+                   const float* bias, const void* residual, int64_t ldr, void* out, int64_t ldo,
+                   int32_t M, int32_t N, int32_t K, int32_t out_dtype, int32_t act, void* stream);
+
 /* Variable-length (ragged) prefill over packed segments, TOKEN_MAJOR
  * (T, H, 64) operands and output.  Segment s owns query rows
  * [cu_seqlens_q[s], cu_seqlens_q[s+1]) and keys [cu_seqlens_k[s],

@@ -64,6 +64,7 @@ def lib():
             "ora_int8_quantize": ([_f32p, i, i, i, ctypes.c_void_p, _f32p, _f32p], i),
             "ora_int8_gemv": ([_f32p, i, ctypes.c_void_p, _f32p, _f32p, i, i, i, _f32p, i], None),
             "ora_f16_round": ([_f32p, ctypes.c_longlong, ctypes.c_void_p], None),
+            "ora_fast_gelu": ([_f32p, _f32p, ctypes.c_longlong], None),
             "ora_f16_serves": ([i], i),
             "ora_f16_gemv": ([_f32p, i, ctypes.c_void_p, _f32p, i, i, _f32p, i], None),
         }
@@ -318,4 +319,16 @@ def f16_gemv(x, w16, bias=None, threads=None):
     lib().ora_f16_gemv(_p(x), x.shape[0], w16.ctypes.data_as(ctypes.c_void_p),
                        None if b is None else _p(b), rows, cols, _p(out), threads or default_threads())
     return out
+
+
+# --------------------------------------------------------------------------
+# FastGelu (text_decoder.rs gelu_scalar), restated in fast_gelu_ref.cpp
+# --------------------------------------------------------------------------
+
+def fast_gelu(x):
+    """gelu_scalar elementwise, f32 in, f32 out."""
+    x = _f32(x)
+    y = np.empty_like(x)
+    lib().ora_fast_gelu(_p(x), _p(y), x.size)
+    return y
 
