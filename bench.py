@@ -512,6 +512,51 @@ def bench_f16_gemv(steps: int, dev):
     return res
 
 
+def bench_projections(steps: int, dev):
+    """The encoder's projections around the attention through the fused GEMM
+    (`ffai_b200.gemm.linear`), on one c4 segment batch's tokens (16 segments x
+    1500 frames, large-v3): q/k/v (N 3840), out-projection + residual, fc1 +
+    FastGelu, fc2 + residual; TFLOP/s against the measured bf16 peak, beside
+    torch's cuBLAS linear on the same operands (no fused epilogue)."""
+    import torch
+
+    from ffai_b200.gemm import linear
+    g = torch.Generator(device=dev).manual_seed(17)
+    T, D = 16 * 1500, 1280
+    res = {}
+
+    def time_it(fn, reps):
+        for _ in range(3):
+            fn()
+        torch.cuda.synchronize()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        for _ in range(reps):
+            fn()
+        b.record()
+        torch.cuda.synchronize()
+        return a.elapsed_time(b) / 1e3 / reps
+
+    x = torch.randn(T, D, device=dev, generator=g).to(torch.bfloat16)
+    h = torch.randn(T, 4 * D, device=dev, generator=g).to(torch.bfloat16)
+    resid = torch.randn(T, D, device=dev, generator=g)
+    cases = (("qkv", x, 3 * D, None, None), ("out_proj_residual", x, D, None, resid),
+             ("fc1_fast_gelu", x, 4 * D, "fast_gelu", None), ("fc2_residual", h, D, None, resid))
+    for name, a, n, act, r in cases:
+        k = a.shape[1]
+        w = (torch.randn(n, k, device=dev, generator=g) / k ** 0.5).to(torch.bfloat16)
+        bias = torch.randn(n, device=dev, generator=g)
+        out_dtype = torch.float32 if r is not None else torch.bfloat16
+        out = torch.empty(T, n, device=dev, dtype=out_dtype)
+        t = time_it(lambda: linear(a, w, bias, act, r, out_dtype=out_dtype, out=out), max(3, steps))
+        tb = time_it(lambda: torch.nn.functional.linear(a, w, bias.to(torch.bfloat16)), max(3, steps))
+        flop = 2.0 * T * n * k
+        res[name] = {"kernel": "gemm_tc_kernel", "m_n_k": [T, n, k], "us": round(t * 1e6, 1),
+                     "tflops": round(flop / t / 1e12, 1),
+                     "torch_linear_tflops": round(flop / tb / 1e12, 1)}
+    return res
+
+
 def bench_ragged(dist, steps: int, peaks):
     """c5: 256 packed segments of U{200..1500} frames, 16 heads, through the
     varlen entry; segments assigned to ranks longest-processing-time first on
@@ -692,6 +737,12 @@ def run_ours(args, dist):
         for v_ in decode.values():
             v_["frac_of_hbm"] = round(v_["gbs_graph"] / peaks["hbm_gbs"], 4)
 
+    proj = None
+    if dist.rank == 0 and not args.no_gemm:
+        proj = bench_projections(max(5, min(args.steps, 20)), torch.device("cuda", torch.cuda.current_device()))
+        for v_ in proj.values():
+            v_["frac_of_peak"] = round(v_["tflops"] / peaks["bf16_tflops"], 4)
+
     f16 = None
     if dist.rank == 0 and not args.no_f16:
         f16 = bench_f16_gemv(max(5, min(args.steps, 50)), torch.device("cuda", torch.cuda.current_device()))
@@ -745,6 +796,7 @@ def run_ours(args, dist):
             "ragged_c5": ragged,
             "int8_gemv": int8,
             "f16_gemv": f16,
+            "encoder_projections": proj,
         }
         print(json.dumps(line), flush=True)
     dist.barrier()
@@ -762,6 +814,7 @@ def main():
     ap.add_argument("--no-ragged", action="store_true")
     ap.add_argument("--no-int8", action="store_true")
     ap.add_argument("--no-f16", action="store_true")
+    ap.add_argument("--no-gemm", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--segments", type=int, default=0,
