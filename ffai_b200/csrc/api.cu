@@ -1567,9 +1567,14 @@ int ffai_gemm_bf16(ffai_attn_ctx* ctx, const void* a, int64_t lda, const void* b
   if (st) return st;
   st = make_map_2d(ctx, &tmb, b, K, N, ldb, 256);
   if (st) return st;
-  CUtensorMap tmo;  // 32 x 32 output blocks for the epilogue's TMA stores
+  CUtensorMap tmo, tmr;  // 32 x 32 output / residual blocks of the epilogue's TMA copies
   st = make_map_2d(ctx, &tmo, out, N, M, ldo, 32, out_dtype == FFAI_DT_F32, 32);
   if (st) return st;
+  tmr = tmo;
+  if (residual) {
+    st = make_map_2d(ctx, &tmr, residual, N, M, ldr, 32, out_dtype == FFAI_DT_F32, 32);
+    if (st) return st;
+  }
   GemmParams p{};
   p.M = M;
   p.N = N;
@@ -1584,7 +1589,7 @@ int ffai_gemm_bf16(ffai_attn_ctx* ctx, const void* a, int64_t lda, const void* b
   p.out_f32 = out_dtype == FFAI_DT_F32;
   p.act = act;
   p.err = ctx->d_err;
-  FFAI_CUDA(ctx, launch_gemm(tma, tmb, tmo, p, ctx->num_sms, static_cast<cudaStream_t>(stream)));
+  FFAI_CUDA(ctx, launch_gemm(tma, tmb, tmo, tmr, p, ctx->num_sms, static_cast<cudaStream_t>(stream)));
   return FFAI_ATTN_OK;
 }
 

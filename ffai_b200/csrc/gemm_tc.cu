@@ -33,6 +33,10 @@ constexpr int kGmStages = 4;
 constexpr int kGmABytes = kGmBM * kGmBK * 2;   // 16 KB
 constexpr int kGmBBytes = kGmBN * kGmBK * 2;   // 32 KB
 constexpr int kGmStageBytes = kGmABytes + kGmBBytes;
+#ifndef FFAI_GM_GELU_UNROLL
+#define FFAI_GM_GELU_UNROLL 32
+#endif
+constexpr int kGmGeluUnroll = FFAI_GM_GELU_UNROLL;
 constexpr int kGmEpiWarps = 8;
 constexpr int kGmEpiCols = kGmBN / (kGmEpiWarps / 4);  // columns per epilogue warp
 // Per epilogue warp, the staging of its 32 x 32 output blocks for the TMA
@@ -46,6 +50,7 @@ struct GmBars {
   uint64_t full[kGmStages], empty[kGmStages];
   uint64_t acc_full[2], acc_empty[2];
   uint64_t done;
+  uint64_t res[kGmEpiWarps];  // per epilogue warp: its residual block has landed
   uint32_t tmem_base;
   int abort_flag;
 };
@@ -89,7 +94,8 @@ __device__ __forceinline__ void bulk_wait_read_1() {
 
 __global__ void __launch_bounds__(kGmThreads, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                   const __grid_constant__ CUtensorMap tmO, GemmParams p) {
+                   const __grid_constant__ CUtensorMap tmO, const __grid_constant__ CUtensorMap tmR,
+                   GemmParams p) {
   extern __shared__ uint8_t dsm_raw[];
   // 1024-byte alignment for the 128-byte swizzle atoms
   uint8_t* dsm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(dsm_raw) + 1023) & ~uintptr_t(1023));
@@ -110,6 +116,7 @@ __global__ void __launch_bounds__(kGmThreads, 1)
       mbar_init(&bars->acc_empty[i], kGmEpiWarps);
     }
     mbar_init(&bars->done, 1);
+    for (int i = 0; i < kGmEpiWarps; ++i) mbar_init(&bars->res[i], 1);
     bars->abort_flag = 0;
     fence_mbar_init();
   }
@@ -199,7 +206,9 @@ __global__ void __launch_bounds__(kGmThreads, 1)
     griddep_wait();
     const int lg = warp & 3, ch = warp >> 2;
     uint8_t* stg = stage_out + warp * kGmStageOut;
-    uint32_t stores = 0;
+    uint32_t stores = 0, res_loads = 0;
+    const bool has_res = p.residual != nullptr;
+    const uint32_t blk_bytes = p.out_f32 ? 4096u : 2048u;
     uint32_t ti = 0;
     for (int t = blockIdx.x; t < tiles; t += gridDim.x, ++ti) {
       const uint32_t acc = ti & 1;
@@ -208,12 +217,26 @@ __global__ void __launch_bounds__(kGmThreads, 1)
       tc_fence_after();
       const int tm = t / p.n_tiles, tn = t - tm * p.n_tiles;
       const int row0 = tm * kGmBM + 32 * lg;
-      const long long row = static_cast<long long>(row0) + lane;
       for (int c0 = 0; c0 < kGmEpiCols; c0 += 32) {
+        const int n0 = tn * kGmBN + kGmEpiCols * ch + c0;
+        // this block's staging buffer; its previous TMA store must have read it
+        uint8_t* buf = p.out_f32 ? stg : stg + (stores & 1) * 2048;
+        if (n0 < p.N) {
+          if (lane == 0) {
+            if (p.out_f32)
+              bulk_wait_read_all();
+            else
+              bulk_wait_read_1();
+            if (has_res) {  // the residual block lands in the buffer the output leaves from
+              mbar_arrive_expect_tx(&bars->res[warp], blk_bytes);
+              tma_load_2d(buf, &tmR, &bars->res[warp], n0, row0);
+            }
+          }
+          __syncwarp();
+        }
         uint32_t r[32];
         tmem_ld32(tmem + acc * kGmBN + (static_cast<uint32_t>(32 * lg) << 16) + kGmEpiCols * ch + c0, r);
         tmem_wait_ld();
-        const int n0 = tn * kGmBN + kGmEpiCols * ch + c0;
         if (n0 >= p.N) continue;  // warp-uniform; N % 32 == 0
         float v[32];
 #pragma unroll
@@ -231,68 +254,60 @@ __global__ void __launch_bounds__(kGmThreads, 1)
           }
         }
         if (p.act == 1) {
-#pragma unroll
+#pragma unroll kGmGeluUnroll
           for (int i = 0; i < 32; ++i) v[i] = fast_gelu(v[i]);
         }
-        const bool has_row = row < p.M;
+        if (has_res &&
+            !mbar_wait(&bars->res[warp], res_loads & 1, abort_flag, p.err, kErrTimeoutConsumer)) {
+          ++res_loads;
+          break;
+        }
+        if (has_res) ++res_loads;
         if (p.out_f32) {
-          if (p.residual != nullptr && has_row) {
-            const float* res = static_cast<const float*>(p.residual) + row * p.ldr + n0;
-#pragma unroll
-            for (int i = 0; i < 32; i += 4) {
-              const float4 q = *reinterpret_cast<const float4*>(res + i);
-              v[i] = __fadd_rn(v[i], q.x);
-              v[i + 1] = __fadd_rn(v[i + 1], q.y);
-              v[i + 2] = __fadd_rn(v[i + 2], q.z);
-              v[i + 3] = __fadd_rn(v[i + 3], q.w);
-            }
-          }
           // 128-byte rows, 128-byte swizzle: 16-byte unit k of row r at k ^ (r % 8)
-          if (lane == 0) bulk_wait_read_all();
-          __syncwarp();
 #pragma unroll
-          for (int k = 0; k < 8; ++k)
-            *reinterpret_cast<float4*>(stg + lane * 128 + ((k ^ (lane & 7)) << 4)) =
-                make_float4(v[4 * k], v[4 * k + 1], v[4 * k + 2], v[4 * k + 3]);
-          fence_proxy_async_smem();
-          __syncwarp();
-          if (lane == 0) {
-            tma_store_2d(&tmO, stg, n0, row0);
-            bulk_commit();
+          for (int k = 0; k < 8; ++k) {
+            float4* q = reinterpret_cast<float4*>(buf + lane * 128 + ((k ^ (lane & 7)) << 4));
+            float4 w = make_float4(v[4 * k], v[4 * k + 1], v[4 * k + 2], v[4 * k + 3]);
+            if (has_res) {
+              const float4 rr = *q;
+              w.x = __fadd_rn(w.x, rr.x);
+              w.y = __fadd_rn(w.y, rr.y);
+              w.z = __fadd_rn(w.z, rr.z);
+              w.w = __fadd_rn(w.w, rr.w);
+            }
+            *q = w;
           }
         } else {
-          if (p.residual != nullptr && has_row) {
-            const uint16_t* res = static_cast<const uint16_t*>(p.residual) + row * p.ldr + n0;
-#pragma unroll
-            for (int i = 0; i < 32; i += 8) {
-              const uint4 q = *reinterpret_cast<const uint4*>(res + i);
-              const uint32_t qq[4] = {q.x, q.y, q.z, q.w};
-#pragma unroll
-              for (int e = 0; e < 4; ++e) {
-                v[i + 2 * e] = __fadd_rn(v[i + 2 * e], lo_half(qq[e], 0));
-                v[i + 2 * e + 1] = __fadd_rn(v[i + 2 * e + 1], hi_half(qq[e], 0));
-              }
-            }
-          }
-          // two buffers; 64-byte rows, 64-byte swizzle: unit k of row r at k ^ ((r / 2) % 4)
-          uint8_t* buf = stg + (stores & 1) * 2048;
-          if (lane == 0) bulk_wait_read_1();  // the store that used this buffer has read it
-          __syncwarp();
+          // 64-byte rows, 64-byte swizzle: unit k of row r at k ^ ((r / 2) % 4)
 #pragma unroll
           for (int k = 0; k < 4; ++k) {
+            uint4* q = reinterpret_cast<uint4*>(buf + lane * 64 + ((k ^ ((lane >> 1) & 3)) << 4));
+            float w[8];
+#pragma unroll
+            for (int e = 0; e < 8; ++e) w[e] = v[8 * k + e];
+            if (has_res) {
+              const uint4 rr = *q;
+              const uint32_t qq[4] = {rr.x, rr.y, rr.z, rr.w};
+#pragma unroll
+              for (int e = 0; e < 4; ++e) {
+                w[2 * e] = __fadd_rn(w[2 * e], lo_half(qq[e], 0));
+                w[2 * e + 1] = __fadd_rn(w[2 * e + 1], hi_half(qq[e], 0));
+              }
+            }
             uint4 pk;
-            pk.x = pack_bf16x2(v[8 * k], v[8 * k + 1]);
-            pk.y = pack_bf16x2(v[8 * k + 2], v[8 * k + 3]);
-            pk.z = pack_bf16x2(v[8 * k + 4], v[8 * k + 5]);
-            pk.w = pack_bf16x2(v[8 * k + 6], v[8 * k + 7]);
-            *reinterpret_cast<uint4*>(buf + lane * 64 + ((k ^ ((lane >> 1) & 3)) << 4)) = pk;
+            pk.x = pack_bf16x2(w[0], w[1]);
+            pk.y = pack_bf16x2(w[2], w[3]);
+            pk.z = pack_bf16x2(w[4], w[5]);
+            pk.w = pack_bf16x2(w[6], w[7]);
+            *q = pk;
           }
-          fence_proxy_async_smem();
-          __syncwarp();
-          if (lane == 0) {
-            tma_store_2d(&tmO, buf, n0, row0);
-            bulk_commit();
-          }
+        }
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+          tma_store_2d(&tmO, buf, n0, row0);
+          bulk_commit();
         }
         ++stores;
       }
@@ -316,7 +331,7 @@ __global__ void __launch_bounds__(kGmThreads, 1)
 size_t gemm_smem_bytes() { return kGmSmem; }
 
 cudaError_t launch_gemm(const CUtensorMap& tmA, const CUtensorMap& tmB, const CUtensorMap& tmO,
-                        const GemmParams& p, int sms, cudaStream_t s) {
+                        const CUtensorMap& tmR, const GemmParams& p, int sms, cudaStream_t s) {
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return e;
@@ -339,7 +354,7 @@ cudaError_t launch_gemm(const CUtensorMap& tmA, const CUtensorMap& tmB, const CU
   cfg.stream = s;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  e = cudaLaunchKernelEx(&cfg, gemm_tc_kernel, tmA, tmB, tmO, p);
+  e = cudaLaunchKernelEx(&cfg, gemm_tc_kernel, tmA, tmB, tmO, tmR, p);
   if (e != cudaSuccess) return e;
   return cudaGetLastError();
 }

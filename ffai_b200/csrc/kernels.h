@@ -196,7 +196,7 @@ struct GemmParams {
 };
 size_t gemm_smem_bytes();
 cudaError_t launch_gemm(const CUtensorMap& tmA, const CUtensorMap& tmB, const CUtensorMap& tmO,
-                        const GemmParams& p, int sms, cudaStream_t s);
+                        const CUtensorMap& tmR, const GemmParams& p, int sms, cudaStream_t s);
 
 // ---- checked f32 prefill (prefill_simt.cu) ---------------------------------
 
