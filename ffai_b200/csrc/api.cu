@@ -1589,6 +1589,8 @@ int ffai_gemm_bf16(ffai_attn_ctx* ctx, const void* a, int64_t lda, const void* b
   p.out_f32 = out_dtype == FFAI_DT_F32;
   p.act = act;
   p.err = ctx->d_err;
+  p.f2_one = 0x3F8000003F800000ull;
+  p.f2_neg_zero = 0x8000000080000000ull;
   FFAI_CUDA(ctx, launch_gemm(tma, tmb, tmo, tmr, p, ctx->num_sms, static_cast<cudaStream_t>(stream)));
   return FFAI_ATTN_OK;
 }

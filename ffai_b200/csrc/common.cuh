@@ -417,6 +417,33 @@ __device__ __forceinline__ uint64_t f2_add(uint64_t a, uint64_t b) {
   return d;
 }
 
+// A separately rounded f32x2 multiply and add, for arithmetic that must
+// match another machine's bit for bit.  ptxas fuses mul.rn.f32x2 followed by
+// add.rn.f32x2 into one fused multiply-add (measured: the rounding of the
+// product disappears), and it does the same to an FMA whose third operand is
+// the constant -0 or whose second is the constant 1.  So these are FMAs with
+// a neutral operand that the caller passes in from memory (a kernel
+// parameter: (-0, -0) and (1, 1)), which ptxas cannot fold: a * b + (-0) and
+// a * 1 + b round exactly like the multiply and the add.
+__device__ __forceinline__ uint64_t f2_mul_rn(uint64_t a, uint64_t b, uint64_t neg_zero) {
+  uint64_t d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(neg_zero));
+  return d;
+}
+
+__device__ __forceinline__ uint64_t f2_add_rn(uint64_t a, uint64_t b, uint64_t one) {
+  uint64_t d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(one), "l"(b));
+  return d;
+}
+
+// MUFU reciprocal, within one ulp of 1 / x (not correctly rounded).
+__device__ __forceinline__ float rcp_approx(float x) {
+  float y;
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
 __device__ __forceinline__ uint64_t f2_sub(uint64_t a, uint64_t b) {
   uint64_t d;
   asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));

@@ -33,10 +33,6 @@ constexpr int kGmStages = 4;
 constexpr int kGmABytes = kGmBM * kGmBK * 2;   // 16 KB
 constexpr int kGmBBytes = kGmBN * kGmBK * 2;   // 32 KB
 constexpr int kGmStageBytes = kGmABytes + kGmBBytes;
-#ifndef FFAI_GM_GELU_UNROLL
-#define FFAI_GM_GELU_UNROLL 32
-#endif
-constexpr int kGmGeluUnroll = FFAI_GM_GELU_UNROLL;
 constexpr int kGmEpiWarps = 8;
 constexpr int kGmEpiCols = kGmBN / (kGmEpiWarps / 4);  // columns per epilogue warp
 // Per epilogue warp, the staging of its 32 x 32 output blocks for the TMA
@@ -57,19 +53,70 @@ struct GmBars {
 constexpr size_t kGmSmem =
     1024 + kGmStages * kGmStageBytes + kGmEpiWarps * kGmStageOut + sizeof(GmBars) + 64;
 
-// Whisper's GELU as the reference computes it (gelu_scalar): a Pade 7/8
-// tanh, every operation a separately rounded f32 multiply or add.
-__device__ __forceinline__ float fast_gelu(float t) {
-  const float u = __fmul_rn(0.7978846f, __fmaf_rn(__fmul_rn(__fmul_rn(0.044715f, t), t), t, t));
-  const float u2 = fminf(__fmul_rn(u, u), 64.0f);
-  const float num = __fmul_rn(
-      u, __fadd_rn(135135.0f,
-                   __fmul_rn(u2, __fadd_rn(17325.0f, __fmul_rn(u2, __fadd_rn(378.0f, u2))))));
-  const float den = __fadd_rn(
-      135135.0f,
-      __fmul_rn(u2, __fadd_rn(62370.0f, __fmul_rn(u2, __fadd_rn(3150.0f, __fmul_rn(u2, 28.0f))))));
-  const float r = fminf(fmaxf(__fdiv_rn(num, den), -1.0f), 1.0f);
-  return __fmul_rn(__fmul_rn(0.5f, t), __fadd_rn(1.0f, r));
+// One element of the division num / den in fast_gelu2, rounded to nearest
+// even without a division instruction.  q1n is the negated quotient, within
+// one ulp of it, r1 = num + q1n den its exact remainder; cn is q1n moved one
+// ulp towards the true quotient (the sign of r1 says which side it lies on),
+// rc its exact remainder, and the closer of the two (smaller |remainder|)
+// is the rounded quotient.  A quotient of two f32 is never exactly halfway
+// between two f32 (the midpoint has 25 significant bits, num only 24), so
+// there is no tie.  A NaN (num infinite or NaN) falls back to num * (-1/den).
+__device__ __forceinline__ float div_pick(float q1n, float r1, float rc_of_cn, float cn, float q0n) {
+  float x = fabsf(rc_of_cn) < fabsf(r1) ? cn : q1n;
+  return x != x ? q0n : x;
+}
+__device__ __forceinline__ float div_neighbour(float q1n, float r1) {
+  const uint32_t grow = (__float_as_uint(r1) ^ __float_as_uint(q1n)) >> 31;
+  return __uint_as_float(__float_as_uint(q1n) + 2u * grow - 1u);
+}
+
+// Whisper's GELU as the reference computes it (gelu_scalar,
+// text_decoder.rs:341-350), two elements at a time with f32x2 arithmetic:
+//   u = 0.7978846 * mul_add(0.044715 t t, t, t),  u2 = min(u u, 64)
+//   num = u (135135 + u2 (17325 + u2 (378 + u2)))
+//   den = 135135 + u2 (62370 + u2 (3150 + u2 28))
+//   out = 0.5 t (1 + clamp(num / den, -1, 1))
+// Every operation is the same separately rounded f32 operation as the
+// reference's, in the same order.  The division is the correctly rounded
+// quotient, reached without a division instruction (den >= 135135 is
+// normal): a MUFU reciprocal y of -den, the negated quotient q0n = num y,
+// one residual correction q1n = q0n + (num + q0n den) y, which lands within
+// one ulp of the quotient (y's error of about 2^-23 enters squared), then
+// div_pick.  The remainders num + q den are exact f32 values whenever q is
+// within one ulp of the quotient, so the fused multiply-adds compute them
+// without error.  Quotients below 2^-25 in magnitude (where the remainders
+// may underflow) leave 1 + clamp(..) = 1 whatever their last bits.
+__device__ __forceinline__ void fast_gelu2(float& t0, float& t1, uint64_t k1, uint64_t kz) {
+  const uint64_t t = f2_pack(t0, t1);
+  const uint64_t c = f2_fma(f2_mul_rn(f2_mul_rn(f2_pack(0.044715f, 0.044715f), t, kz), t, kz), t, t);
+  const uint64_t u = f2_mul_rn(f2_pack(0.7978846f, 0.7978846f), c, kz);
+  float a0, a1;
+  f2_unpack(f2_mul_rn(u, u, kz), a0, a1);
+  const uint64_t u2 = f2_pack(fminf(a0, 64.0f), fminf(a1, 64.0f));
+  uint64_t n = f2_add_rn(f2_pack(378.0f, 378.0f), u2, k1);
+  n = f2_add_rn(f2_pack(17325.0f, 17325.0f), f2_mul_rn(u2, n, kz), k1);
+  n = f2_add_rn(f2_pack(135135.0f, 135135.0f), f2_mul_rn(u2, n, kz), k1);
+  n = f2_mul_rn(u, n, kz);
+  uint64_t d = f2_mul_rn(u2, f2_pack(28.0f, 28.0f), kz);
+  d = f2_add_rn(f2_pack(3150.0f, 3150.0f), d, k1);
+  d = f2_add_rn(f2_pack(62370.0f, 62370.0f), f2_mul_rn(u2, d, kz), k1);
+  d = f2_add_rn(f2_pack(135135.0f, 135135.0f), f2_mul_rn(u2, d, kz), k1);
+  float d0, d1;
+  f2_unpack(d, d0, d1);
+  const uint64_t ny = f2_pack(rcp_approx(-d0), rcp_approx(-d1));
+  const uint64_t q0n = f2_mul_rn(n, ny, kz);
+  const uint64_t q1n = f2_fma(f2_fma(q0n, d, n), ny, q0n);
+  const uint64_t r1 = f2_fma(q1n, d, n);
+  float qa, qb, ra, rb, pa, pb;
+  f2_unpack(q1n, qa, qb);
+  f2_unpack(r1, ra, rb);
+  f2_unpack(q0n, pa, pb);
+  const float ca = div_neighbour(qa, ra), cb = div_neighbour(qb, rb);
+  float sa, sb;
+  f2_unpack(f2_fma(f2_pack(ca, cb), d, n), sa, sb);
+  const float xa = -div_pick(qa, ra, sa, ca, pa), xb = -div_pick(qb, rb, sb, cb, pb);
+  const uint64_t r = f2_pack(fminf(fmaxf(xa, -1.0f), 1.0f), fminf(fmaxf(xb, -1.0f), 1.0f));
+  f2_unpack(f2_mul_rn(f2_mul_rn(f2_pack(0.5f, 0.5f), t, kz), f2_add_rn(f2_pack(1.0f, 1.0f), r, k1), kz), t0, t1);
 }
 
 __device__ __forceinline__ void tma_load_2d(void* smem_dst, const CUtensorMap* map, uint64_t* bar,
@@ -254,8 +301,8 @@ __global__ void __launch_bounds__(kGmThreads, 1)
           }
         }
         if (p.act == 1) {
-#pragma unroll kGmGeluUnroll
-          for (int i = 0; i < 32; ++i) v[i] = fast_gelu(v[i]);
+#pragma unroll
+          for (int i = 0; i < 32; i += 2) fast_gelu2(v[i], v[i + 1], p.f2_one, p.f2_neg_zero);
         }
         if (has_res &&
             !mbar_wait(&bars->res[warp], res_loads & 1, abort_flag, p.err, kErrTimeoutConsumer)) {

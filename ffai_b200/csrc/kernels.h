@@ -193,6 +193,10 @@ struct GemmParams {
   int out_f32;
   int act;
   unsigned* err;
+  // f32x2 pairs (1, 1) and (-0, -0), read by the epilogue's activation as
+  // runtime operands: written as constants, ptxas folds them and fuses the
+  // activation's separately rounded multiplies and adds.
+  unsigned long long f2_one, f2_neg_zero;
 };
 size_t gemm_smem_bytes();
 cudaError_t launch_gemm(const CUtensorMap& tmA, const CUtensorMap& tmB, const CUtensorMap& tmO,

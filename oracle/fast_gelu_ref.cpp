@@ -18,10 +18,10 @@ void ora_fast_gelu(const float* x, float* y, long long n) {
   for (long long i = 0; i < n; ++i) {
     const float t = x[i];
     const float u = 0.7978846f * std::fmaf(0.044715f * t * t, t, t);
-    const float u2 = std::min(u * u, 64.0f);
+    const float u2 = std::fmin(u * u, 64.0f);  // Rust f32::min: a NaN yields the other operand
     const float num = u * (135135.0f + u2 * (17325.0f + u2 * (378.0f + u2)));
     const float den = 135135.0f + u2 * (62370.0f + u2 * (3150.0f + u2 * 28.0f));
-    const float r = std::min(std::max(num / den, -1.0f), 1.0f);
+    const float r = std::min(std::max(num / den, -1.0f), 1.0f);  // NaN stays NaN, as Rust clamp
     y[i] = 0.5f * t * (1.0f + r);
   }
 }

@@ -59,6 +59,16 @@ def test_gemm_matches_fp32_reference(oracle, M, N, K, variant, out_dtype):
     assert err <= tol, f"max relative error {err:.3e}"
 
 
+def _assert_bits_equal(got, want, x):
+    """Bit-for-bit, NaN where the reference gives NaN; names the first misses."""
+    nan = np.isnan(want)
+    bad = (np.isnan(got) != nan) | (~nan & (got.view(np.int32) != want.view(np.int32)))
+    idx = np.argwhere(bad)[:8]
+    assert not bad.any(), (f"{int(bad.sum())} mismatches, first: "
+                           + ", ".join(f"t={x[tuple(i)]!r} got={got[tuple(i)]!r} "
+                                       f"want={want[tuple(i)]!r}" for i in idx))
+
+
 @pytest.mark.gpu
 def test_gemm_epilogue_fast_gelu_bit_exact(oracle):
     # a[m][0] = t_m, b[n][0] = 1: the accumulator is t_m exactly; bias b_n
@@ -74,7 +84,33 @@ def test_gemm_epilogue_fast_gelu_bit_exact(oracle):
     got = linear(a.to(DEV), w.to(DEV), bias.to(DEV), "fast_gelu", out_dtype=torch.float32)
     x = (t.float()[:, None] + bias[None, :]).numpy().astype(np.float32)
     want = oracle.fast_gelu(x)
-    assert np.array_equal(got.cpu().numpy().view(np.int32), want.view(np.int32))
+    _assert_bits_equal(got.cpu().numpy(), want, x)
+
+
+@pytest.mark.gpu
+def test_gemm_epilogue_fast_gelu_bit_exact_wide(oracle):
+    # ~1M pre-activations t_m + b_n spread over every binade from 1e-30 to
+    # 1e12 of both signs (plus +-inf and zero), through the epilogue's
+    # division-free rounding of num / den: bit for bit, NaN where the
+    # reference gives NaN
+    from ffai_b200.gemm import linear
+    M, N, K = 256, 4096, 8
+    g = np.random.default_rng(11)
+    t = torch.from_numpy(np.concatenate([np.linspace(-6, 6, M - 16), np.zeros(16)])
+                         .astype(np.float32)).to(torch.bfloat16)
+    a = torch.zeros(M, K, dtype=torch.bfloat16)
+    a[:, 0] = t
+    w = torch.zeros(N, K, dtype=torch.bfloat16)
+    w[:, 0] = 1
+    mag = 10.0 ** g.uniform(-30, 12, N)
+    bias = (mag * g.choice([-1.0, 1.0], N)).astype(np.float32)
+    bias[:4] = [np.inf, -np.inf, 0.0, -0.0]
+    bias[4:1024] = g.uniform(-8, 8, 1020).astype(np.float32)  # the rational's own range
+    got = linear(a.to(DEV), w.to(DEV), torch.from_numpy(bias).to(DEV), "fast_gelu",
+                 out_dtype=torch.float32).cpu().numpy()
+    x = (t.float()[:, None] + torch.from_numpy(bias)[None, :]).numpy().astype(np.float32)
+    want = oracle.fast_gelu(x)
+    _assert_bits_equal(got, want, x)
 
 
 @pytest.mark.gpu
