@@ -12,11 +12,13 @@
 //
 // B200 structure: persistent CTAs, one per SM, over 128 x 256 output tiles
 // (all n-tiles of an m-tile adjacent, so the activation tile stays in L2).
-// Warp 8 is the TMA producer (4-stage ring of 128 x 64 A and 256 x 64 B
-// tiles, 128-byte swizzle), warp 9 issues tcgen05.mma (M = 128, N = 256,
-// K = 16 steps) into one of two TMEM accumulators, so the epilogue of a tile
-// overlaps the main loop of the next; warps 0-7 are the epilogue (warp w
-// reads TMEM lanes 32 (w % 4) .., columns 128 (w / 4) ..).  Every wait is
+// Warps 0..E-1 are the epilogue (E = 8, or 12 for a bf16 output with the
+// activation; warp w reads TMEM lanes 32 (w % 4) .. and every (E / 4)-th
+// 32-column chunk from 32 (w / 4)), warp E is the TMA producer (4-stage ring
+// of 128 x 64 A and 256 x 64 B tiles, 128-byte swizzle), warp E + 1 issues
+// tcgen05.mma (M = 128, N = 256, K = 16 steps) into one of two TMEM
+// accumulators, so the epilogue of a tile overlaps the main loop of the
+// next.  Every wait is
 // bounded; on a time-out the CTA drains its copies and MMAs, frees TMEM and
 // leaves an error bit.
 #include <atomic>
@@ -33,25 +35,35 @@ constexpr int kGmStages = 4;
 constexpr int kGmABytes = kGmBM * kGmBK * 2;   // 16 KB
 constexpr int kGmBBytes = kGmBN * kGmBK * 2;   // 32 KB
 constexpr int kGmStageBytes = kGmABytes + kGmBBytes;
-constexpr int kGmEpiWarps = 8;
-constexpr int kGmEpiCols = kGmBN / (kGmEpiWarps / 4);  // columns per epilogue warp
+// Epilogue warps: 8 (two per scheduler), or 12 for a bf16 output with the
+// activation, whose dependent f32 chains need a third warp per scheduler to
+// keep the tensor core busy.  Warp w reads TMEM lanes 32 (w % 4) .. and the
+// 32-column chunks j, j + E / 4, j + 2 E / 4, ... of the tile (j = w / 4).
+constexpr int kGmMaxEpiWarps = 12;
 // Per epilogue warp, the staging of its 32 x 32 output blocks for the TMA
-// store: one f32 block or two bf16 blocks (double-buffered).
-constexpr int kGmStageOut = 4096;
-constexpr int kGmProducer = kGmEpiWarps, kGmMma = kGmEpiWarps + 1;
-constexpr int kGmThreads = (kGmEpiWarps + 2) * 32;
+// store: with 8 epilogue warps one f32 block or two bf16 blocks
+// (double-buffered), with 12 one bf16 block (shared memory is full).
+template <int E>
+struct GmCfg {
+  static constexpr int kStageOut = E == 8 ? 4096 : 2048;
+  static constexpr int kProducer = E, kMma = E + 1;
+  static constexpr int kThreads = (E + 2) * 32;
+};
 constexpr int kGmTmemCols = 2 * kGmBN;  // two accumulators
 
 struct GmBars {
   uint64_t full[kGmStages], empty[kGmStages];
   uint64_t acc_full[2], acc_empty[2];
   uint64_t done;
-  uint64_t res[kGmEpiWarps];  // per epilogue warp: its residual block has landed
+  uint64_t res[kGmMaxEpiWarps];  // per epilogue warp: its residual block has landed
   uint32_t tmem_base;
   int abort_flag;
 };
-constexpr size_t kGmSmem =
-    1024 + kGmStages * kGmStageBytes + kGmEpiWarps * kGmStageOut + sizeof(GmBars) + 64;
+template <int E>
+constexpr size_t gm_smem() {
+  return 1024 + kGmStages * kGmStageBytes + E * GmCfg<E>::kStageOut + sizeof(GmBars) + 64;
+}
+static_assert(gm_smem<8>() <= 227 * 1024 && gm_smem<12>() <= 227 * 1024, "shared memory");
 
 // One element of the division num / den in fast_gelu2, rounded to nearest
 // even without a division instruction.  q1n is the negated quotient, within
@@ -139,7 +151,8 @@ __device__ __forceinline__ void bulk_wait_read_1() {
   asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory");
 }
 
-__global__ void __launch_bounds__(kGmThreads, 1)
+template <int E>
+__global__ void __launch_bounds__(GmCfg<E>::kThreads, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                    const __grid_constant__ CUtensorMap tmO, const __grid_constant__ CUtensorMap tmR,
                    GemmParams p) {
@@ -147,7 +160,9 @@ __global__ void __launch_bounds__(kGmThreads, 1)
   // 1024-byte alignment for the 128-byte swizzle atoms
   uint8_t* dsm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(dsm_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* stage_out = dsm + kGmStages * kGmStageBytes;
-  GmBars* bars = reinterpret_cast<GmBars*>(stage_out + kGmEpiWarps * kGmStageOut);
+  constexpr int kStageOut = GmCfg<E>::kStageOut;
+  constexpr int kGmProducer = GmCfg<E>::kProducer, kGmMma = GmCfg<E>::kMma;
+  GmBars* bars = reinterpret_cast<GmBars*>(stage_out + E * kStageOut);
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   const int tiles = p.m_tiles * p.n_tiles;
   const int kblocks = (p.K + kGmBK - 1) / kGmBK;
@@ -160,10 +175,10 @@ __global__ void __launch_bounds__(kGmThreads, 1)
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&bars->acc_full[i], 1);
-      mbar_init(&bars->acc_empty[i], kGmEpiWarps);
+      mbar_init(&bars->acc_empty[i], E);
     }
     mbar_init(&bars->done, 1);
-    for (int i = 0; i < kGmEpiWarps; ++i) mbar_init(&bars->res[i], 1);
+    for (int i = 0; i < E; ++i) mbar_init(&bars->res[i], 1);
     bars->abort_flag = 0;
     fence_mbar_init();
   }
@@ -245,14 +260,16 @@ __global__ void __launch_bounds__(kGmThreads, 1)
       mbar_wait(&bars->done, 0, &none, p.err, kErrTimeoutDrain);
     }
   } else {
-    // Epilogue: warp w, TMEM lanes 32 (w % 4) + i = tile row, columns
-    // kGmEpiCols (w / 4) + [0, kGmEpiCols).  Each 32 x 32 block goes through
+    // Epilogue: warp w, TMEM lanes 32 (w % 4) + i = tile row, the 32-column
+    // chunks w / 4 + (E / 4) k of the tile.  Each 32 x 32 block goes through
     // a swizzled shared-memory staging buffer to one TMA store (rows past M
     // are clipped by the store).  The residual and the output may belong to
     // the preceding kernel.
     griddep_wait();
     const int lg = warp & 3, ch = warp >> 2;
-    uint8_t* stg = stage_out + warp * kGmStageOut;
+    uint8_t* stg = stage_out + warp * kStageOut;
+    // two bf16 blocks in flight per warp where the staging holds them
+    const bool dbuf = kStageOut == 4096 && !p.out_f32;
     uint32_t stores = 0, res_loads = 0;
     const bool has_res = p.residual != nullptr;
     const uint32_t blk_bytes = p.out_f32 ? 4096u : 2048u;
@@ -264,16 +281,16 @@ __global__ void __launch_bounds__(kGmThreads, 1)
       tc_fence_after();
       const int tm = t / p.n_tiles, tn = t - tm * p.n_tiles;
       const int row0 = tm * kGmBM + 32 * lg;
-      for (int c0 = 0; c0 < kGmEpiCols; c0 += 32) {
-        const int n0 = tn * kGmBN + kGmEpiCols * ch + c0;
+      for (int c0 = 32 * ch; c0 < kGmBN; c0 += 32 * (E / 4)) {
+        const int n0 = tn * kGmBN + c0;
         // this block's staging buffer; its previous TMA store must have read it
-        uint8_t* buf = p.out_f32 ? stg : stg + (stores & 1) * 2048;
+        uint8_t* buf = dbuf ? stg + (stores & 1) * 2048 : stg;
         if (n0 < p.N) {
           if (lane == 0) {
-            if (p.out_f32)
-              bulk_wait_read_all();
-            else
+            if (dbuf)
               bulk_wait_read_1();
+            else
+              bulk_wait_read_all();
             if (has_res) {  // the residual block lands in the buffer the output leaves from
               mbar_arrive_expect_tx(&bars->res[warp], blk_bytes);
               tma_load_2d(buf, &tmR, &bars->res[warp], n0, row0);
@@ -282,7 +299,7 @@ __global__ void __launch_bounds__(kGmThreads, 1)
           __syncwarp();
         }
         uint32_t r[32];
-        tmem_ld32(tmem + acc * kGmBN + (static_cast<uint32_t>(32 * lg) << 16) + kGmEpiCols * ch + c0, r);
+        tmem_ld32(tmem + acc * kGmBN + (static_cast<uint32_t>(32 * lg) << 16) + c0, r);
         tmem_wait_ld();
         if (n0 >= p.N) continue;  // warp-uniform; N % 32 == 0
         float v[32];
@@ -375,18 +392,21 @@ __global__ void __launch_bounds__(kGmThreads, 1)
 
 }  // namespace
 
-size_t gemm_smem_bytes() { return kGmSmem; }
+size_t gemm_smem_bytes() { return gm_smem<8>() > gm_smem<12>() ? gm_smem<8>() : gm_smem<12>(); }
 
-cudaError_t launch_gemm(const CUtensorMap& tmA, const CUtensorMap& tmB, const CUtensorMap& tmO,
-                        const CUtensorMap& tmR, const GemmParams& p, int sms, cudaStream_t s) {
+namespace {
+
+template <int E>
+cudaError_t launch_gemm_e(const CUtensorMap& tmA, const CUtensorMap& tmB, const CUtensorMap& tmO,
+                          const CUtensorMap& tmR, const GemmParams& p, int sms, cudaStream_t s) {
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return e;
   static std::atomic<bool> configured[64];
   if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
   if (!configured[dev].load(std::memory_order_acquire)) {
-    e = cudaFuncSetAttribute(gemm_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             static_cast<int>(kGmSmem));
+    e = cudaFuncSetAttribute(gemm_tc_kernel<E>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             static_cast<int>(gm_smem<E>()));
     if (e != cudaSuccess) return e;
     configured[dev].store(true, std::memory_order_release);
   }
@@ -396,14 +416,22 @@ cudaError_t launch_gemm(const CUtensorMap& tmA, const CUtensorMap& tmB, const CU
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cudaLaunchConfig_t cfg{};
   cfg.gridDim = dim3(static_cast<unsigned>(tiles < sms ? tiles : sms));
-  cfg.blockDim = dim3(kGmThreads);
-  cfg.dynamicSmemBytes = kGmSmem;
+  cfg.blockDim = dim3(GmCfg<E>::kThreads);
+  cfg.dynamicSmemBytes = gm_smem<E>();
   cfg.stream = s;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  e = cudaLaunchKernelEx(&cfg, gemm_tc_kernel, tmA, tmB, tmO, tmR, p);
+  e = cudaLaunchKernelEx(&cfg, gemm_tc_kernel<E>, tmA, tmB, tmO, tmR, p);
   if (e != cudaSuccess) return e;
   return cudaGetLastError();
+}
+
+}  // namespace
+
+cudaError_t launch_gemm(const CUtensorMap& tmA, const CUtensorMap& tmB, const CUtensorMap& tmO,
+                        const CUtensorMap& tmR, const GemmParams& p, int sms, cudaStream_t s) {
+  if (p.act == 1 && !p.out_f32) return launch_gemm_e<12>(tmA, tmB, tmO, tmR, p, sms, s);
+  return launch_gemm_e<8>(tmA, tmB, tmO, tmR, p, sms, s);
 }
 
 }  // namespace ffai
