@@ -870,8 +870,10 @@ int ffai_attn_prefill_host(ffai_attn_ctx* ctx, const ffai_attn_desc* d, const vo
   const size_t lb = lse ? static_cast<size_t>(H) * Nq * sizeof(float) : 0;
   if (lse && d->out_layout == FFAI_LAYOUT_TOKEN_MAJOR)
     return set_error(ctx, FFAI_ATTN_DECLINED, "host prefill: lse needs heads-split output");
-  // Chunks of sequences, two slots in flight.
-  const int chunk = std::max(1, std::min(B, (B + 3) / 4));
+  // Chunks of sequences (about an eighth of the batch: the first chunk's
+  // copy-in and the last chunk's kernel and copy-out are the part that does
+  // not overlap), two slots in flight.
+  const int chunk = std::max(1, std::min(B, (B + 7) / 8));
   const size_t slot = chunk * (qb + 2 * kb + ob + lb);
   const size_t slot_al = (slot + 255) / 256 * 256;
   st = ensure(ctx, reinterpret_cast<uint8_t**>(&ctx->d_pipe), &ctx->pipe_cap, 2 * slot_al);
