@@ -17,7 +17,9 @@
 // row; the reduction is four shuffles.  A lane keeps its chain for 4 rows and
 // a warp takes 8 rows, so an activation value loaded from shared memory
 // feeds 4 rows (shared-memory traffic, not HBM, is what limits several
-// activation rows).  Weights are stored [8-row group][16-column step][column]
+// activation rows).  Where a matrix has few groups for its width (the
+// tall, narrow fc2 and out-projection), 2 or 4 warps share a group, each
+// taking 2 or 1 of a lane's 4 rows: more chains in flight, same layout.  Weights are stored [8-row group][16-column step][column]
 // [8 rows], so a lane's 4 rows are one 8-byte load, a warp's step 256
 // contiguous bytes and a run of a group's steps one bulk copy.  Streaming
 // as in the int8 GEMV (gemv_int8.cu): persistent CTAs over contiguous group
@@ -27,6 +29,7 @@
 // through L1.
 #include <algorithm>
 #include <atomic>
+#include <type_traits>
 
 #include <cuda_fp16.h>
 
@@ -79,8 +82,11 @@ __global__ void f16_pack_kernel(const T* w, int rows, int cols, uint16_t* packed
 
 // XS: the activations staged in shared memory, chain-major ([row b][chain c]
 // [step j], a lane's next 4 steps one 16-byte load); else read through L1.
-template <int NB, bool XS>
+// LR: rows per lane (4 or 2), i.e. 4 / LR warps per group.
+template <int NB, bool XS, int LR>
 __global__ void __launch_bounds__(kHgThreads, 1) f16_gemv_kernel(F16GemvParams p) {
+  constexpr int Q = kHgLaneRows / LR;          // warps per group
+  constexpr int kGpr = kHgConsWarps / Q;       // groups per round
   const F16GemvPlan& P = p.plan;
   extern __shared__ __align__(128) uint8_t dsm[];
   uint64_t* full = reinterpret_cast<uint64_t*>(dsm + P.bar_off);
@@ -98,7 +104,7 @@ __global__ void __launch_bounds__(kHgThreads, 1) f16_gemv_kernel(F16GemvParams p
   if (tid == 0) {
     for (int i = 0; i < ring; ++i) {
       mbar_init(&full[i], 1);
-      mbar_init(&empty[i], 1);  // the warp that owns the unit's group
+      mbar_init(&empty[i], Q);  // the warps that own the unit's group
       s_use[i] = -1;
     }
     s_abort = 0;
@@ -114,7 +120,7 @@ __global__ void __launch_bounds__(kHgThreads, 1) f16_gemv_kernel(F16GemvParams p
     if (lane >= ring) return;
     uint64_t* fb = &full[lane];
     const int units = (g_end - g_begin) * upg;
-    const int full_round = kHgConsWarps * upg;
+    const int full_round = kGpr * upg;
     int issued = 0;
     bool ok = true;
     for (int j = lane; j < units; j += ring, ++issued) {
@@ -123,8 +129,8 @@ __global__ void __launch_bounds__(kHgThreads, 1) f16_gemv_kernel(F16GemvParams p
         ok = false;
         break;
       }
-      const int ro = j / full_round, g0 = g_begin + ro * kHgConsWarps;
-      const int n = min(kHgConsWarps, g_end - g0), rem = j - ro * full_round;
+      const int ro = j / full_round, g0 = g_begin + ro * kGpr;
+      const int n = min(kGpr, g_end - g0), rem = j - ro * full_round;
       const int k = rem / n, i = rem - k * n;
       const uint32_t bytes = static_cast<uint32_t>(min(S, steps - k * S)) * kHgStepBytes;
       *reinterpret_cast<volatile int*>(&s_use[lane]) = issued;
@@ -145,15 +151,52 @@ __global__ void __launch_bounds__(kHgThreads, 1) f16_gemv_kernel(F16GemvParams p
   // Lane (r, c): chain c of row r of the warp's group.  A step past `cols`
   // (the 8-column tail) is taken by chains 0-7 only, as the reference's
   // tail loop feeds only its first accumulator.
-  const int r = lane >> 4, c = lane & 15;  // rows 4 r .. 4 r + 3 of the group
+  // rows 4 r + LR q .. + LR - 1 of the warp's group gi
+  const int r = lane >> 4, c = lane & 15, gi = warp / Q, q = warp - gi * Q;
   const bool tail8 = (cols & 15) != 0;
   const float* xb = p.x + c;
   float* xt = reinterpret_cast<float*>(dsm + P.x_off);
   const int pitch = P.x_pitch;  // floats per (row, chain); a multiple of 4, odd / 4
   if constexpr (XS) {
-    for (int i = tid; i < NB * cols; i += kHgConsWarps * 32) {
-      const int b = i / cols, col = i - b * cols;
-      xt[(b * 16 + (col & 15)) * pitch + (col >> 4)] = p.x[i];
+    // Item (b, quad, c): chain c's steps 4 quad .. 4 quad + 3 of activation
+    // row b, gathered (a half-warp reads 64 contiguous bytes per step) into
+    // one 16-byte store.  Items are walked without division; two items'
+    // loads are in flight before their stores.
+    constexpr int kStride = kHgConsWarps * 32;
+    const int per_b = 16 * ((steps + 3) / 4), total = NB * per_b;
+    auto gather = [&](int b, int rem, float (&v)[4]) {
+      const float* xr = p.x + static_cast<size_t>(b) * cols + (rem & 15) + 64 * (rem >> 4);
+#pragma unroll
+      for (int u = 0; u < 4; ++u) v[u] = 64 * (rem >> 4) + 16 * u + (rem & 15) < cols ? xr[16 * u] : 0.f;
+    };
+    auto put = [&](int b, int rem, const float (&v)[4]) {
+      *reinterpret_cast<float4*>(xt + (b * 16 + (rem & 15)) * pitch + 4 * (rem >> 4)) =
+          make_float4(v[0], v[1], v[2], v[3]);
+    };
+    auto advance = [&](int& b, int& rem) {
+      rem += kStride;
+      while (rem >= per_b) {
+        rem -= per_b;
+        ++b;
+      }
+    };
+    int b0 = 0, r0 = tid;
+    while (r0 >= per_b) {
+      r0 -= per_b;
+      ++b0;
+    }
+    for (int i = tid; i < total; i += 2 * kStride) {
+      int b1 = b0, r1 = r0;
+      advance(b1, r1);
+      float v0[4], v1[4];
+      gather(b0, r0, v0);
+      const bool two = i + kStride < total;
+      if (two) gather(b1, r1, v1);
+      put(b0, r0, v0);
+      if (two) put(b1, r1, v1);
+      b0 = b1;
+      r0 = r1;
+      advance(b0, r0);
     }
     named_bar_sync(1, kHgConsWarps * 32);
   }
@@ -165,20 +208,20 @@ __global__ void __launch_bounds__(kHgThreads, 1) f16_gemv_kernel(F16GemvParams p
       return __ldg(xb + static_cast<size_t>(b) * cols + 16 * step);
   };
   int j0 = 0;  // stream index of the round's first unit
-  for (int g0 = g_begin; g0 < g_end; g0 += kHgConsWarps) {
-    const int n = min(kHgConsWarps, g_end - g0);
-    if (warp >= n) {
+  for (int g0 = g_begin; g0 < g_end; g0 += kGpr) {
+    const int n = min(kGpr, g_end - g0);
+    if (gi >= n) {
       j0 += n * upg;
       continue;
     }
-    float acc[NB][kHgLaneRows];
+    float acc[NB][LR];
 #pragma unroll
     for (int b = 0; b < NB; ++b)
 #pragma unroll
-      for (int i = 0; i < kHgLaneRows; ++i) acc[b][i] = 0.f;
+      for (int i = 0; i < LR; ++i) acc[b][i] = 0.f;
     bool ok = true;
     for (int k = 0; k < upg; ++k) {
-      const int j = j0 + k * n + warp, slot = j % ring, use = j / ring;
+      const int j = j0 + k * n + gi, slot = j % ring, use = j / ring;
       if (!wait_slot_use(&s_use[slot], use, &s_abort, p.err) ||
           !mbar_wait(&full[slot], use & 1, &s_abort, p.err, kErrTimeoutConsumer)) {
         ok = false;
@@ -187,38 +230,56 @@ __global__ void __launch_bounds__(kHgThreads, 1) f16_gemv_kernel(F16GemvParams p
       const int s0 = k * S, sk = min(S, steps - s0);
       // the last step of the row, when it is the 8-column tail: chains 0-7
       const int full_steps = (tail8 && s0 + sk == steps) ? sk - 1 : sk;
-      // this lane's 4 rows of column 16 j + c: 8 bytes at step j
-      const uint2* wsl = reinterpret_cast<const uint2*>(dsm + static_cast<size_t>(slot) * P.slot_bytes) +
-                         c * 2 + r;
-      auto wrow = [&](int step, float (&wv)[kHgLaneRows]) {
-        const uint2 h = wsl[step * (kHgStepHalves / 4)];
-        const float2 lo = __half22float2(*reinterpret_cast<const __half2*>(&h.x));
-        const float2 hi = __half22float2(*reinterpret_cast<const __half2*>(&h.y));
-        wv[0] = lo.x;
-        wv[1] = lo.y;
-        wv[2] = hi.x;
-        wv[3] = hi.y;
+      // this lane's LR rows of column 16 j + c: 2 LR bytes at step j
+      const __half* wsl = reinterpret_cast<const __half*>(dsm + static_cast<size_t>(slot) * P.slot_bytes) +
+                          c * kHgRows + kHgLaneRows * r + LR * q;
+      auto wrow = [&](int step, float (&wv)[LR]) {
+        const __half* h = wsl + step * kHgStepHalves;
+        if constexpr (LR == 4) {
+          const uint2 u = *reinterpret_cast<const uint2*>(h);
+          const float2 lo = __half22float2(*reinterpret_cast<const __half2*>(&u.x));
+          const float2 hi = __half22float2(*reinterpret_cast<const __half2*>(&u.y));
+          wv[0] = lo.x;
+          wv[1] = lo.y;
+          wv[2] = hi.x;
+          wv[3] = hi.y;
+        } else {
+          static_assert(LR == 2, "rows per lane");
+          const float2 f = __half22float2(*reinterpret_cast<const __half2*>(h));
+          wv[0] = f.x;
+          wv[1] = f.y;
+        }
       };
       int t = 0;
       if constexpr (XS) {
-        // s0 and t are multiples of 4: the activations of 4 steps are one float4
-        for (; t + 4 <= full_steps; t += 4) {
-          float wv[4][kHgLaneRows];
+        // s0 and t are multiples of 4: the activations of 4 steps are one
+        // float4.  kXU steps' loads are issued before their FMAs (one or two
+        // warps per scheduler here: the shared-memory latency needs ILP).
+        constexpr int kXU = LR == 2 ? 8 : 4;
+        auto batch = [&](auto xu) {
+          constexpr int U = decltype(xu)::value;
+          float wv[U][LR];
 #pragma unroll
-          for (int u = 0; u < 4; ++u) wrow(t + u, wv[u]);
+          for (int u = 0; u < U; ++u) wrow(t + u, wv[u]);
 #pragma unroll
           for (int b = 0; b < NB; ++b) {
-            const float4 xv = *reinterpret_cast<const float4*>(xl + b * 16 * pitch + s0 + t);
-            const float xs[4] = {xv.x, xv.y, xv.z, xv.w};
 #pragma unroll
-            for (int u = 0; u < 4; ++u)
+            for (int h = 0; h < U / 4; ++h) {
+              const float4 xv = *reinterpret_cast<const float4*>(xl + b * 16 * pitch + s0 + t + 4 * h);
+              const float xs[4] = {xv.x, xv.y, xv.z, xv.w};
 #pragma unroll
-              for (int i = 0; i < kHgLaneRows; ++i) acc[b][i] = __fmaf_rn(wv[u][i], xs[u], acc[b][i]);
+              for (int u = 0; u < 4; ++u)
+#pragma unroll
+                for (int i = 0; i < LR; ++i)
+                  acc[b][i] = __fmaf_rn(wv[4 * h + u][i], xs[u], acc[b][i]);
+            }
           }
-        }
+        };
+        for (; t + kXU <= full_steps; t += kXU) batch(std::integral_constant<int, kXU>{});
+        for (; t + 4 <= full_steps; t += 4) batch(std::integral_constant<int, 4>{});
       } else {
         for (; t + 2 <= full_steps; t += 2) {
-          float wv[2][kHgLaneRows], xv[2][NB];
+          float wv[2][LR], xv[2][NB];
 #pragma unroll
           for (int u = 0; u < 2; ++u) {
             wrow(t + u, wv[u]);
@@ -230,27 +291,27 @@ __global__ void __launch_bounds__(kHgThreads, 1) f16_gemv_kernel(F16GemvParams p
 #pragma unroll
             for (int b = 0; b < NB; ++b)
 #pragma unroll
-              for (int i = 0; i < kHgLaneRows; ++i) acc[b][i] = __fmaf_rn(wv[u][i], xv[u][b], acc[b][i]);
+              for (int i = 0; i < LR; ++i) acc[b][i] = __fmaf_rn(wv[u][i], xv[u][b], acc[b][i]);
         }
       }
       for (; t < full_steps; ++t) {
-        float wv[kHgLaneRows];
+        float wv[LR];
         wrow(t, wv);
 #pragma unroll
         for (int b = 0; b < NB; ++b) {
           const float xv = x1(b, s0 + t);
 #pragma unroll
-          for (int i = 0; i < kHgLaneRows; ++i) acc[b][i] = __fmaf_rn(wv[i], xv, acc[b][i]);
+          for (int i = 0; i < LR; ++i) acc[b][i] = __fmaf_rn(wv[i], xv, acc[b][i]);
         }
       }
       if (full_steps < sk && c < 8) {
-        float wv[kHgLaneRows];
+        float wv[LR];
         wrow(full_steps, wv);
 #pragma unroll
         for (int b = 0; b < NB; ++b) {
           const float xv = x1(b, s0 + full_steps);
 #pragma unroll
-          for (int i = 0; i < kHgLaneRows; ++i) acc[b][i] = __fmaf_rn(wv[i], xv, acc[b][i]);
+          for (int i = 0; i < LR; ++i) acc[b][i] = __fmaf_rn(wv[i], xv, acc[b][i]);
         }
       }
       __syncwarp();
@@ -261,8 +322,8 @@ __global__ void __launch_bounds__(kHgThreads, 1) f16_gemv_kernel(F16GemvParams p
     // ((a0 + a4) + (a2 + a6)) + ((a1 + a5) + (a3 + a7)), a_i = c_i + c_{i+8}:
     // each add is of a pair of lanes, and IEEE addition is commutative
 #pragma unroll
-    for (int i = 0; i < kHgLaneRows; ++i) {
-      const int row = (g0 + warp) * kHgRows + kHgLaneRows * r + i;
+    for (int i = 0; i < LR; ++i) {
+      const int row = (g0 + gi) * kHgRows + kHgLaneRows * r + LR * q + i;
       const float bias = (p.bias != nullptr && row < p.rows) ? __ldg(p.bias + row) : 0.f;
 #pragma unroll
       for (int b = 0; b < NB; ++b) {
@@ -278,10 +339,25 @@ __global__ void __launch_bounds__(kHgThreads, 1) f16_gemv_kernel(F16GemvParams p
   }
 }
 
+template <int NB, int LR>
+cudaError_t launch_nb_lr(const F16GemvParams& p, cudaLaunchConfig_t& cfg) {
+  return p.plan.x_pitch > 0 ? cudaLaunchKernelEx(&cfg, f16_gemv_kernel<NB, true, LR>, p)
+                            : cudaLaunchKernelEx(&cfg, f16_gemv_kernel<NB, false, LR>, p);
+}
+
 template <int NB>
 cudaError_t launch_nb(const F16GemvParams& p, cudaLaunchConfig_t& cfg) {
-  return p.plan.x_pitch > 0 ? cudaLaunchKernelEx(&cfg, f16_gemv_kernel<NB, true>, p)
-                            : cudaLaunchKernelEx(&cfg, f16_gemv_kernel<NB, false>, p);
+  return p.plan.q == 2 ? launch_nb_lr<NB, 2>(p, cfg) : launch_nb_lr<NB, 4>(p, cfg);
+}
+
+template <int NB>
+cudaError_t configure_nb() {
+  for (auto fn : {f16_gemv_kernel<NB, true, 4>, f16_gemv_kernel<NB, false, 4>,
+                  f16_gemv_kernel<NB, true, 2>, f16_gemv_kernel<NB, false, 2>}) {
+    const cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, kHgSmemMax);
+    if (e != cudaSuccess) return e;
+  }
+  return cudaSuccess;
 }
 
 }  // namespace
@@ -293,6 +369,13 @@ bool f16_gemv_plan(int rows, int cols, int batch, int sms, F16GemvPlan* plan) {
   const long long groups = f16_gemv_groups(rows);
   P.groups = static_cast<int>(groups);
   P.grid = static_cast<int>(std::min<long long>(sms, groups));
+  // Two warps per group where that leaves the number of rounds of the
+  // busiest CTA unchanged (the extra warps would otherwise idle).  Measured
+  // on the decoder's shapes: 2 beats 1 by 4-22 %; 4 loses to 2 everywhere
+  // (each warp's 2-byte loads and conversions outweigh the extra chains).
+  const int gpc = static_cast<int>((groups + P.grid - 1) / P.grid);
+  auto rounds = [&](int q) { return (gpc + kHgConsWarps / q - 1) / (kHgConsWarps / q); };
+  P.q = rounds(2) == rounds(1) ? 2 : 1;
   const int steps = f16_gemv_steps(cols);
   const int upg = std::max(1, (steps * kHgStepBytes + kHgSlotTarget - 1) / kHgSlotTarget);
   P.S = ((steps + upg - 1) / upg + 3) / 4 * 4;  // a multiple of 4 steps
@@ -342,7 +425,7 @@ cudaError_t launch_f16_pack(const void* w, int w_dtype, int rows, int cols, uint
 cudaError_t launch_f16_gemv(const F16GemvParams& p, cudaStream_t s) {
   const F16GemvPlan& P = p.plan;
   if (p.batch < 1 || p.batch > kHgMaxBatch || !f16_gemv_served(p.cols) || P.smem > kHgSmemMax ||
-      P.ring < 2 || P.ring > kHgMaxRing)
+      P.ring < 2 || P.ring > kHgMaxRing || (P.q != 1 && P.q != 2))
     return cudaErrorInvalidValue;
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
@@ -350,13 +433,9 @@ cudaError_t launch_f16_gemv(const F16GemvParams& p, cudaStream_t s) {
   static std::atomic<bool> configured[64];
   if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
   if (!configured[dev].load(std::memory_order_acquire)) {
-    for (auto fn : {f16_gemv_kernel<1, true>, f16_gemv_kernel<2, true>, f16_gemv_kernel<3, true>,
-                    f16_gemv_kernel<4, true>, f16_gemv_kernel<5, true>, f16_gemv_kernel<6, true>,
-                    f16_gemv_kernel<7, true>, f16_gemv_kernel<8, true>, f16_gemv_kernel<1, false>,
-                    f16_gemv_kernel<2, false>, f16_gemv_kernel<3, false>, f16_gemv_kernel<4, false>,
-                    f16_gemv_kernel<5, false>, f16_gemv_kernel<6, false>, f16_gemv_kernel<7, false>,
-                    f16_gemv_kernel<8, false>}) {
-      e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, kHgSmemMax);
+    for (auto cfg_fn : {configure_nb<1>, configure_nb<2>, configure_nb<3>, configure_nb<4>,
+                        configure_nb<5>, configure_nb<6>, configure_nb<7>, configure_nb<8>}) {
+      e = cfg_fn();
       if (e != cudaSuccess) return e;
     }
     configured[dev].store(true, std::memory_order_release);

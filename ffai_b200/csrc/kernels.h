@@ -152,10 +152,12 @@ __host__ __device__ inline int f16_gemv_steps(int cols) { return (cols + 15) / 1
 inline bool f16_gemv_served(int cols) { return cols > 0 && cols % 8 == 0 && cols <= kHgMaxCols; }
 
 // Launch geometry (host): as for the int8 GEMV -- CTA c takes a contiguous
-// range of groups in rounds of one group per consumer warp, each group cut
-// into units of S steps streamed unit-major through `ring` slots.
+// range of groups in rounds, each group cut into units of S steps streamed
+// unit-major through `ring` slots.  q warps (1, 2 or 4) share a group, each
+// taking 4 / q of every lane's 4 rows; a round is consumer warps / q groups.
 struct F16GemvPlan {
   int groups, grid, ring, S;
+  int q;           // warps per group
   int slot_bytes;  // S * 64
   int bar_off, x_off, x_pitch, smem;  // x_pitch 0: activations read through L1
 };
