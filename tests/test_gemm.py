@@ -40,7 +40,7 @@ def _ref(a, w, bias, act, residual, oracle):
     (1500, 5120, 1280), (1500, 1280, 5120), (3000, 3840, 1280), (1500, 1280, 1280),
     (200, 384, 384), (129, 288, 72), (1, 32, 8),
 ])
-@pytest.mark.parametrize("variant", ["plain", "bias_gelu", "bias_residual"])
+@pytest.mark.parametrize("variant", ["plain", "bias_gelu", "bias_residual", "bias_gelu_residual"])
 @pytest.mark.parametrize("out_dtype", [torch.float32, torch.bfloat16])
 def test_gemm_matches_fp32_reference(oracle, M, N, K, variant, out_dtype):
     from ffai_b200.gemm import linear
@@ -48,8 +48,8 @@ def test_gemm_matches_fp32_reference(oracle, M, N, K, variant, out_dtype):
     a = torch.randn(M, K, device=DEV, generator=g).to(torch.bfloat16)
     w = (torch.randn(N, K, device=DEV, generator=g) / K ** 0.5).to(torch.bfloat16)
     bias = torch.randn(N, device=DEV, generator=g) if variant != "plain" else None
-    act = "fast_gelu" if variant == "bias_gelu" else None
-    res = torch.randn(M, N, device=DEV, generator=g).to(out_dtype) if variant == "bias_residual" else None
+    act = "fast_gelu" if "gelu" in variant else None
+    res = torch.randn(M, N, device=DEV, generator=g).to(out_dtype) if "residual" in variant else None
     got = linear(a, w, bias, act, res, out_dtype=out_dtype)
     torch.cuda.synchronize()
     want = _ref(a, w, bias, act, res, oracle)
@@ -88,11 +88,13 @@ def test_gemm_epilogue_fast_gelu_bit_exact(oracle):
 
 
 @pytest.mark.gpu
-def test_gemm_epilogue_fast_gelu_bit_exact_wide(oracle):
+@pytest.mark.parametrize("out_dtype", [torch.float32, torch.bfloat16])
+def test_gemm_epilogue_fast_gelu_bit_exact_wide(oracle, out_dtype):
     # ~1M pre-activations t_m + b_n spread over every binade from 1e-30 to
     # 1e12 of both signs (plus +-inf and zero), through the epilogue's
     # division-free rounding of num / den: bit for bit, NaN where the
-    # reference gives NaN
+    # reference gives NaN; f32 output (8 epilogue warps) and bf16 output
+    # (12 epilogue warps, the value rounded to nearest even)
     from ffai_b200.gemm import linear
     M, N, K = 256, 4096, 8
     g = np.random.default_rng(11)
@@ -107,9 +109,11 @@ def test_gemm_epilogue_fast_gelu_bit_exact_wide(oracle):
     bias[:4] = [np.inf, -np.inf, 0.0, -0.0]
     bias[4:1024] = g.uniform(-8, 8, 1020).astype(np.float32)  # the rational's own range
     got = linear(a.to(DEV), w.to(DEV), torch.from_numpy(bias).to(DEV), "fast_gelu",
-                 out_dtype=torch.float32).cpu().numpy()
+                 out_dtype=out_dtype).float().cpu().numpy()
     x = (t.float()[:, None] + torch.from_numpy(bias)[None, :]).numpy().astype(np.float32)
     want = oracle.fast_gelu(x)
+    if out_dtype == torch.bfloat16:  # the bf16 store rounds to nearest even
+        want = torch.from_numpy(want).to(torch.bfloat16).float().numpy()
     _assert_bits_equal(got, want, x)
 
 
