@@ -270,7 +270,7 @@ __global__ void __launch_bounds__(GmCfg<E>::kThreads, 1)
     uint8_t* stg = stage_out + warp * kStageOut;
     // two bf16 blocks in flight per warp where the staging holds them
     const bool dbuf = kStageOut == 4096 && !p.out_f32;
-    uint32_t stores = 0, res_loads = 0;
+    uint32_t stores = 0, res_loads = 0, res_issued = 0;
     const bool has_res = p.residual != nullptr;
     const uint32_t blk_bytes = p.out_f32 ? 4096u : 2048u;
     uint32_t ti = 0;
@@ -296,6 +296,7 @@ __global__ void __launch_bounds__(GmCfg<E>::kThreads, 1)
               tma_load_2d(buf, &tmR, &bars->res[warp], n0, row0);
             }
           }
+          if (has_res) ++res_issued;
           __syncwarp();
         }
         uint32_t r[32];
@@ -321,12 +322,11 @@ __global__ void __launch_bounds__(GmCfg<E>::kThreads, 1)
 #pragma unroll
           for (int i = 0; i < 32; i += 2) fast_gelu2(v[i], v[i + 1], p.f2_one, p.f2_neg_zero);
         }
-        if (has_res &&
-            !mbar_wait(&bars->res[warp], res_loads & 1, abort_flag, p.err, kErrTimeoutConsumer)) {
+        if (has_res) {
+          if (!mbar_wait(&bars->res[warp], res_loads & 1, abort_flag, p.err, kErrTimeoutConsumer))
+            break;
           ++res_loads;
-          break;
         }
-        if (has_res) ++res_loads;
         if (p.out_f32) {
           // 128-byte rows, 128-byte swizzle: 16-byte unit k of row r at k ^ (r % 8)
 #pragma unroll
@@ -378,6 +378,10 @@ __global__ void __launch_bounds__(GmCfg<E>::kThreads, 1)
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&bars->acc_empty[acc]);
+    }
+    if (res_loads < res_issued) {  // an abort: the residual block in flight lands first
+      int none = 0;
+      mbar_wait(&bars->res[warp], res_loads & 1, &none, p.err, kErrTimeoutDrain);
     }
     if (lane == 0) bulk_wait_all();  // the output is written before the CTA ends
   }
