@@ -180,23 +180,43 @@ __global__ void __launch_bounds__(kHgThreads, 1) f16_gemv_kernel(F16GemvParams p
         ++b;
       }
     };
-    int b0 = 0, r0 = tid;
-    while (r0 >= per_b) {
-      r0 -= per_b;
-      ++b0;
-    }
-    for (int i = tid; i < total; i += 2 * kStride) {
-      int b1 = b0, r1 = r0;
-      advance(b1, r1);
-      float v0[4], v1[4];
-      gather(b0, r0, v0);
-      const bool two = i + kStride < total;
-      if (two) gather(b1, r1, v1);
-      put(b0, r0, v0);
-      if (two) put(b1, r1, v1);
-      b0 = b1;
-      r0 = r1;
-      advance(b0, r0);
+    if ((reinterpret_cast<uintptr_t>(p.x) & 15) == 0) {
+      // 16-byte loads of 4 consecutive columns (4 chains of one step), all
+      // activation rows' loads in flight before the scattered 4-byte stores
+      for (int j = tid; j < cols / 4; j += kStride) {
+        float4 v[NB];
+#pragma unroll
+        for (int b = 0; b < NB; ++b)
+          v[b] = *reinterpret_cast<const float4*>(p.x + static_cast<size_t>(b) * cols + 4 * j);
+        const int step = j >> 2, c0 = (4 * j) & 15;
+#pragma unroll
+        for (int b = 0; b < NB; ++b) {
+          float* d = xt + (b * 16 + c0) * pitch + step;
+          d[0] = v[b].x;
+          d[pitch] = v[b].y;
+          d[2 * pitch] = v[b].z;
+          d[3 * pitch] = v[b].w;
+        }
+      }
+    } else {
+      int b0 = 0, r0 = tid;
+      while (r0 >= per_b) {
+        r0 -= per_b;
+        ++b0;
+      }
+      for (int i = tid; i < total; i += 2 * kStride) {
+        int b1 = b0, r1 = r0;
+        advance(b1, r1);
+        float v0[4], v1[4];
+        gather(b0, r0, v0);
+        const bool two = i + kStride < total;
+        if (two) gather(b1, r1, v1);
+        put(b0, r0, v0);
+        if (two) put(b1, r1, v1);
+        b0 = b1;
+        r0 = r1;
+        advance(b0, r0);
+      }
     }
     named_bar_sync(1, kHgConsWarps * 32);
   }

@@ -154,6 +154,23 @@ def test_gemv_matches_oracle(oracle, rows, cols, batch, with_bias):
 
 
 @pytest.mark.gpu
+@pytest.mark.parametrize("rows,cols,batch", [(1280, 5120, 5), (3840, 1280, 1), (33, 24, 3)])
+def test_gemv_unaligned_activations(oracle, rows, cols, batch):
+    # activations 4 bytes past a 16-byte boundary: staged with 4-byte loads
+    from ffai_b200.f16_gemv import F16Gemv
+    w = _weights(rows, cols, rows * cols + 3)
+    rng = np.random.default_rng(cols + batch)
+    x = rng.standard_normal((batch, cols), dtype=np.float32)
+    q = F16Gemv.new(torch.from_numpy(w).to(DEV))
+    buf = torch.empty(batch * cols + 1, device=DEV)
+    xd = buf[1:].view(batch, cols)
+    xd.copy_(torch.from_numpy(x))
+    assert xd.data_ptr() % 16 == 4
+    got = q.forward(xd).cpu().numpy()
+    assert _same(got, oracle.f16_gemv(x, oracle.f16_weights(w)))
+
+
+@pytest.mark.gpu
 def test_gemv_nonfinite_inputs(oracle):
     from ffai_b200.f16_gemv import F16Gemv
     w = _weights(6, 40, 1)
