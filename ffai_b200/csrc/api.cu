@@ -1567,7 +1567,7 @@ int ffai_gemm_bf16(ffai_attn_ctx* ctx, const void* a, int64_t lda, const void* b
   CUtensorMap tma, tmb;
   int st = make_map_2d(ctx, &tma, a, K, M, lda, 128);
   if (st) return st;
-  st = make_map_2d(ctx, &tmb, b, K, N, ldb, 256);
+  st = make_map_2d(ctx, &tmb, b, K, N, ldb, 128);  // B tiles as two 128-row boxes
   if (st) return st;
   CUtensorMap tmo, tmr;  // 32 x 32 output / residual blocks of the epilogue's TMA copies
   st = make_map_2d(ctx, &tmo, out, N, M, ldo, 32, out_dtype == FFAI_DT_F32, 32);
@@ -1583,6 +1583,16 @@ int ffai_gemm_bf16(ffai_attn_ctx* ctx, const void* a, int64_t lda, const void* b
   p.K = K;
   p.m_tiles = (M + 127) / 128;
   p.n_tiles = (N + 255) / 256;
+  {
+    // The last wave's tiles (fewer than the SMs) run as 128-column halves
+    // when that still fits one wave: the wave takes half as long.
+    const long long tiles = static_cast<long long>(p.m_tiles) * p.n_tiles;
+    const long long sms = ctx->num_sms;
+    const long long tail = tiles - (tiles - 1) / sms * sms;  // tiles of the last wave
+    const bool split = 2 * tail <= sms;
+    p.split_from = static_cast<int>(split ? tiles - tail : tiles);
+    p.items = static_cast<int>(split ? tiles + tail : tiles);
+  }
   p.bias = bias;
   p.residual = residual;
   p.ldr = ldr;

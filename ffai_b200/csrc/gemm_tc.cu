@@ -51,6 +51,25 @@ struct GmCfg {
 };
 constexpr int kGmTmemCols = 2 * kGmBN;  // two accumulators
 
+// Work item i: tile (tm, tn), and which columns -- half 0: all 256, half 1 /
+// 2: the first / second 128.
+struct GmItem {
+  int tm, tn, half;
+};
+__device__ __forceinline__ GmItem gm_item(const GemmParams& p, int i) {
+  int t = i, h = 0;
+  if (i >= p.split_from) {
+    const int j = i - p.split_from;
+    t = p.split_from + (j >> 1);
+    h = 1 + (j & 1);
+  }
+  GmItem w;
+  w.tm = t / p.n_tiles;
+  w.tn = t - w.tm * p.n_tiles;
+  w.half = h;
+  return w;
+}
+
 struct GmBars {
   uint64_t full[kGmStages], empty[kGmStages];
   uint64_t acc_full[2], acc_empty[2];
@@ -164,7 +183,7 @@ __global__ void __launch_bounds__(GmCfg<E>::kThreads, 1)
   constexpr int kGmProducer = GmCfg<E>::kProducer, kGmMma = GmCfg<E>::kMma;
   GmBars* bars = reinterpret_cast<GmBars*>(stage_out + E * kStageOut);
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
-  const int tiles = p.m_tiles * p.n_tiles;
+  const int items = p.items;
   const int kblocks = (p.K + kGmBK - 1) / kGmBK;
   volatile int* abort_flag = &bars->abort_flag;
 
@@ -199,8 +218,9 @@ __global__ void __launch_bounds__(GmCfg<E>::kThreads, 1)
       prefetch_tensormap(&tmB);
       uint32_t it = 0;
       bool ok = true;
-      for (int t = blockIdx.x; t < tiles && ok; t += gridDim.x) {
-        const int tm = t / p.n_tiles, tn = t - tm * p.n_tiles;
+      for (int t = blockIdx.x; t < items && ok; t += gridDim.x) {
+        const GmItem w = gm_item(p, t);
+        const int tm = w.tm, tn = w.tn;
         for (int kb = 0; kb < kblocks; ++kb, ++it) {
           const uint32_t s = it % kGmStages;
           if (it >= kGmStages &&
@@ -210,9 +230,15 @@ __global__ void __launch_bounds__(GmCfg<E>::kThreads, 1)
             break;
           }
           uint8_t* sa = dsm + s * kGmStageBytes;
-          mbar_arrive_expect_tx(&bars->full[s], kGmStageBytes);
+          // B in two 128-row boxes; a half item loads only its own half
+          // (to the same place as in a whole tile)
+          mbar_arrive_expect_tx(&bars->full[s], w.half ? kGmABytes + kGmBBytes / 2 : kGmStageBytes);
           tma_load_2d(sa, &tmA, &bars->full[s], kb * kGmBK, tm * kGmBM);
-          tma_load_2d(sa + kGmABytes, &tmB, &bars->full[s], kb * kGmBK, tn * kGmBN);
+          if (w.half != 2)
+            tma_load_2d(sa + kGmABytes, &tmB, &bars->full[s], kb * kGmBK, tn * kGmBN);
+          if (w.half != 1)
+            tma_load_2d(sa + kGmABytes + kGmBBytes / 2, &tmB, &bars->full[s], kb * kGmBK,
+                        tn * kGmBN + kGmBN / 2);
         }
       }
       if (!ok || *abort_flag) {
@@ -227,10 +253,16 @@ __global__ void __launch_bounds__(GmCfg<E>::kThreads, 1)
   } else if (warp == kGmMma) {
     if (lane == 0) {
       constexpr uint32_t idesc = idesc_f16(1u, kGmBM, kGmBN, 0, 0);
+      constexpr uint32_t idesc_half = idesc_f16(1u, kGmBM, kGmBN / 2, 0, 0);
       uint32_t it = 0, ti = 0;
       bool ok = true;
-      for (int t = blockIdx.x; t < tiles && ok; t += gridDim.x, ++ti) {
+      for (int t = blockIdx.x; t < items && ok; t += gridDim.x, ++ti) {
         const uint32_t acc = ti & 1;
+        // a half item: N = 128 from B's rows 0-127 or 128-255 (16 KB on, a
+        // whole number of 1 KB swizzle atoms)
+        const int half = gm_item(p, t).half;
+        const uint32_t id = half ? idesc_half : idesc;
+        const uint32_t b_off = half == 2 ? kGmBBytes / 2 : 0;
         if (ti >= 2 && !mbar_wait(&bars->acc_empty[acc], ((ti >> 1) - 1) & 1, abort_flag, p.err,
                                   kErrTimeoutMma)) {
           ok = false;
@@ -245,10 +277,11 @@ __global__ void __launch_bounds__(GmCfg<E>::kThreads, 1)
           }
           tc_fence_after();
           const uint64_t da = smem_desc_sw128(smem_u32(dsm + s * kGmStageBytes), 16, 1024);
-          const uint64_t db = smem_desc_sw128(smem_u32(dsm + s * kGmStageBytes + kGmABytes), 16, 1024);
+          const uint64_t db =
+              smem_desc_sw128(smem_u32(dsm + s * kGmStageBytes + kGmABytes + b_off), 16, 1024);
 #pragma unroll
           for (int k = 0; k < kGmBK / 16; ++k)  // +32 bytes per K step inside the swizzle atom
-            mma_ss(tmem + acc * kGmBN, da + 2 * k, db + 2 * k, idesc, (kb > 0 || k > 0) ? 1u : 0u);
+            mma_ss(tmem + acc * kGmBN, da + 2 * k, db + 2 * k, id, (kb > 0 || k > 0) ? 1u : 0u);
           mma_commit(&bars->empty[s]);
         }
         if (!ok) break;
@@ -274,15 +307,17 @@ __global__ void __launch_bounds__(GmCfg<E>::kThreads, 1)
     const bool has_res = p.residual != nullptr;
     const uint32_t blk_bytes = p.out_f32 ? 4096u : 2048u;
     uint32_t ti = 0;
-    for (int t = blockIdx.x; t < tiles; t += gridDim.x, ++ti) {
+    for (int t = blockIdx.x; t < items; t += gridDim.x, ++ti) {
       const uint32_t acc = ti & 1;
       if (!mbar_wait(&bars->acc_full[acc], (ti >> 1) & 1, abort_flag, p.err, kErrTimeoutConsumer))
         break;
       tc_fence_after();
-      const int tm = t / p.n_tiles, tn = t - tm * p.n_tiles;
-      const int row0 = tm * kGmBM + 32 * lg;
-      for (int c0 = 32 * ch; c0 < kGmBN; c0 += 32 * (E / 4)) {
-        const int n0 = tn * kGmBN + c0;
+      const GmItem w = gm_item(p, t);
+      const int row0 = w.tm * kGmBM + 32 * lg;
+      const int width = w.half ? kGmBN / 2 : kGmBN;  // accumulator columns of the item
+      const int col0 = w.tn * kGmBN + (w.half == 2 ? kGmBN / 2 : 0);
+      for (int c0 = 32 * ch; c0 < width; c0 += 32 * (E / 4)) {
+        const int n0 = col0 + c0;
         // this block's staging buffer; its previous TMA store must have read it
         uint8_t* buf = dbuf ? stg + (stores & 1) * 2048 : stg;
         if (n0 < p.N) {
@@ -414,12 +449,12 @@ cudaError_t launch_gemm_e(const CUtensorMap& tmA, const CUtensorMap& tmB, const 
     if (e != cudaSuccess) return e;
     configured[dev].store(true, std::memory_order_release);
   }
-  const int tiles = p.m_tiles * p.n_tiles;
+  const int items = p.items;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cudaLaunchConfig_t cfg{};
-  cfg.gridDim = dim3(static_cast<unsigned>(tiles < sms ? tiles : sms));
+  cfg.gridDim = dim3(static_cast<unsigned>(items < sms ? items : sms));
   cfg.blockDim = dim3(GmCfg<E>::kThreads);
   cfg.dynamicSmemBytes = gm_smem<E>();
   cfg.stream = s;

@@ -199,6 +199,10 @@ struct GemmParams {
   // runtime operands: written as constants, ptxas folds them and fuses the
   // activation's separately rounded multiplies and adds.
   unsigned long long f2_one, f2_neg_zero;
+  // Work items: tiles [0, split_from) whole, then each tile of [split_from,
+  // m_tiles * n_tiles) as two 128-column halves (the last, partial wave split
+  // so that it runs on twice as many SMs); items = their count.
+  int split_from, items;
 };
 size_t gemm_smem_bytes();
 cudaError_t launch_gemm(const CUtensorMap& tmA, const CUtensorMap& tmB, const CUtensorMap& tmO,
