@@ -11,7 +11,8 @@
 // residual, and stores bf16 or f32.
 //
 // B200 structure: persistent CTAs, one per SM, over 128 x 256 output tiles
-// (all n-tiles of an m-tile adjacent, so the activation tile stays in L2).
+// (all n-tiles of an m-tile adjacent, so the activation tile stays in L2; a
+// short last wave's tiles split into 128-column halves, see gm_item).
 // Warps 0..E-1 are the epilogue (E = 8, or 12 for a bf16 output with the
 // activation; warp w reads TMEM lanes 32 (w % 4) .. and every (E / 4)-th
 // 32-column chunk from 32 (w / 4)), warp E is the TMA producer (4-stage ring
