@@ -108,6 +108,7 @@ SIGNATURES = {
     "ffai_flash_serves": ([_T4P, _T4P], ctypes.c_int),
     "ffai_flash_attend": ([_vp, _T4P, _T4P, _T4P, _i32, _T4P, _vp], ctypes.c_int),
     "ffai_flash_attend_merged": ([_vp, _T4P, _T4P, _T4P, _T4P, _vp], ctypes.c_int),
+    "ffai_flash_check": ([_T4P, _T4P, _T4P, _i32, _i32], ctypes.c_int),
 }
 
 _lib = None

@@ -16,8 +16,9 @@ CSRC = os.path.join(PKG_DIR, "csrc")
 INCLUDE = os.path.join(os.path.dirname(PKG_DIR), "include")
 LIB_PATH = os.path.join(PKG_DIR, "libffai_attn.so")
 
-SOURCES = ["api.cu", "decode.cu", "prefill_simt.cu", "prefill_tc.cu", "convert.cu",
-           "gemv_int8.cu", "gemv_f16.cu", "gemm_tc.cu"]
+# Every CUDA source in csrc/, found by listing it (the Rust crate's build.rs
+# does the same), so no hand-kept list can leave one out.
+SOURCES = sorted(f for f in os.listdir(CSRC) if f.endswith(".cu"))
 NVCC_FLAGS = [
     "-gencode", "arch=compute_100a,code=sm_100a",
     "-O3", "-lineinfo", "-std=c++17",

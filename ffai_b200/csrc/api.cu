@@ -223,6 +223,9 @@ int check_desc(const ffai_attn_ctx* ctx, const ffai_attn_desc* d, int op) {
     if (d->k_layout == FFAI_LAYOUT_TOKEN_MAJOR || d->v_layout != FFAI_LAYOUT_HEADS_SPLIT)
       return set_error(ctx, FFAI_ATTN_DECLINED,
                        "decode: k must be KT or heads-split, v heads-split");
+    // The decode kernels address q and out as dense (row, 64) rows.
+    if (d->token_stride != 0)
+      return set_error(ctx, FFAI_ATTN_DECLINED, "decode: dense q and out only (token_stride 0)");
     return FFAI_ATTN_OK;
   }
   // prefill
@@ -1209,14 +1212,16 @@ int ffai_flash_serves(const ffai_tensor4* kt, const ffai_tensor4* v) {
 
 namespace {
 
-int attend_common(ffai_attn_ctx* ctx, const ffai_tensor4* q, const ffai_tensor4* kt,
-                  const ffai_tensor4* v, int masked, ffai_tensor4* out, bool merged, void* stream) {
-  if (!ctx) return set_error(nullptr, FFAI_ATTN_ERR_INVALID, "null context");
-  if (!q || !kt || !v || !out) return set_error(ctx, FFAI_ATTN_ERR_INVALID, "null tensor");
+// The decline rules of attend / attend_merged (flash_attn.rs:135-158,
+// :218-264) on the operands alone: FFAI_ATTN_OK with `d` filled in for the
+// call, or FFAI_ATTN_DECLINED where the reference returns Ok(None).  Errors
+// and declines are recorded on `ctx` (null: the calling thread).
+int flash_gate(const ffai_attn_ctx* ctx, const ffai_tensor4* q, const ffai_tensor4* kt,
+               const ffai_tensor4* v, int masked, bool merged, ffai_attn_desc* d) {
+  if (!q || !kt || !v) return set_error(ctx, FFAI_ATTN_ERR_INVALID, "null tensor");
   if (masked) return set_error(ctx, FFAI_ATTN_DECLINED, "masked attention is not served");
-  if (q->device != ctx->device || kt->device != ctx->device || v->device != ctx->device ||
-      out->device != ctx->device)
-    return set_error(ctx, FFAI_ATTN_DECLINED, "operands are not on this context's CUDA device");
+  if (q->device < 0 || kt->device != q->device || v->device != q->device)
+    return set_error(ctx, FFAI_ATTN_DECLINED, "operands are not on one CUDA device");
   if (q->dtype != FFAI_DT_F32) return set_error(ctx, FFAI_ATTN_DECLINED, "q must be f32");
   const int64_t b = q->dims[0], heads = q->dims[1], qlen = q->dims[2], hd = q->dims[3];
   if (b != 1 || hd != kHD) return set_error(ctx, FFAI_ATTN_DECLINED, "batch 1, head_dim 64 only");
@@ -1236,19 +1241,31 @@ int attend_common(ffai_attn_ctx* ctx, const ffai_tensor4* q, const ffai_tensor4*
   if (merged ? qlen != keys : (qlen != 1 && qlen != keys))
     return set_error(ctx, FFAI_ATTN_DECLINED, "q_len %lld not served against %lld keys",
                      static_cast<long long>(qlen), static_cast<long long>(keys));
-  if (out->dtype != FFAI_DT_F32) return set_error(ctx, FFAI_ATTN_ERR_INVALID, "out must be f32");
+  ffai_attn_desc_init(d);
+  d->heads = static_cast<int32_t>(heads);
+  d->q_len = static_cast<int32_t>(qlen);
+  d->kv_len = static_cast<int32_t>(keys);
+  d->q_dtype = FFAI_DT_F32;
+  d->kv_dtype = kt->dtype;
+  d->k_layout = FFAI_LAYOUT_KT;
+  d->out_layout = merged ? FFAI_LAYOUT_TOKEN_MAJOR : FFAI_LAYOUT_HEADS_SPLIT;
+  d->scale = 1.0f;  // q arrives pre-scaled (flash_attn.rs:214-217)
+  if (env_on("FFAI_ATTN_CHECKED_F32")) d->flags |= FFAI_ATTN_FLAG_CHECKED_F32;
+  return FFAI_ATTN_OK;
+}
 
+int attend_common(ffai_attn_ctx* ctx, const ffai_tensor4* q, const ffai_tensor4* kt,
+                  const ffai_tensor4* v, int masked, ffai_tensor4* out, bool merged, void* stream) {
+  if (!ctx) return set_error(nullptr, FFAI_ATTN_ERR_INVALID, "null context");
+  if (!q || !kt || !v || !out) return set_error(ctx, FFAI_ATTN_ERR_INVALID, "null tensor");
+  if (q->device != ctx->device || kt->device != ctx->device || v->device != ctx->device ||
+      out->device != ctx->device)
+    return set_error(ctx, FFAI_ATTN_DECLINED, "operands are not on this context's CUDA device");
   ffai_attn_desc d;
-  ffai_attn_desc_init(&d);
-  d.heads = static_cast<int32_t>(heads);
-  d.q_len = static_cast<int32_t>(qlen);
-  d.kv_len = static_cast<int32_t>(keys);
-  d.q_dtype = FFAI_DT_F32;
-  d.kv_dtype = kt->dtype;
-  d.k_layout = FFAI_LAYOUT_KT;
-  d.out_layout = merged ? FFAI_LAYOUT_TOKEN_MAJOR : FFAI_LAYOUT_HEADS_SPLIT;
-  d.scale = 1.0f;  // q arrives pre-scaled (flash_attn.rs:214-217)
-  if (env_on("FFAI_ATTN_CHECKED_F32")) d.flags |= FFAI_ATTN_FLAG_CHECKED_F32;
+  const int st = flash_gate(ctx, q, kt, v, masked, merged, &d);
+  if (st) return st;
+  if (out->dtype != FFAI_DT_F32) return set_error(ctx, FFAI_ATTN_ERR_INVALID, "out must be f32");
+  const int64_t qlen = d.q_len;
   if (qlen == 1 && !merged)
     return ffai_attn_decode(ctx, &d, q->data, kt->data, v->data, out->data, nullptr, 0, stream);
   return ffai_attn_prefill(ctx, &d, q->data, kt->data, v->data, out->data, nullptr, stream);
@@ -1264,6 +1281,12 @@ int ffai_flash_attend(ffai_attn_ctx* ctx, const ffai_tensor4* q, const ffai_tens
 int ffai_flash_attend_merged(ffai_attn_ctx* ctx, const ffai_tensor4* q, const ffai_tensor4* kt,
                              const ffai_tensor4* v, ffai_tensor4* out, void* stream) {
   return attend_common(ctx, q, kt, v, 0, out, true, stream);
+}
+
+int ffai_flash_check(const ffai_tensor4* q, const ffai_tensor4* kt, const ffai_tensor4* v,
+                     int32_t masked, int32_t merged) {
+  ffai_attn_desc d;
+  return flash_gate(nullptr, q, kt, v, masked, merged != 0, &d);
 }
 
 }  // extern "C"
@@ -1368,6 +1391,16 @@ extern "C" int ffai_attn_decode_static(const ffai_attn_desc* d, const void* q, c
   p.scale_log2 = d->scale * 1.4426950408889634f;
   p.counters = static_cast<unsigned*>(base);
   p.part = reinterpret_cast<float*>(static_cast<uint32_t*>(base) + kStaticRows);
+  // The launch reports its status through the runtime's last-error slot, so
+  // an error that earlier, unrelated work left there would be read as this
+  // launch's.  Report it as what it is, without launching and without
+  // clearing it: it belongs to the caller.
+  e = cudaPeekAtLastError();
+  if (e != cudaSuccess)
+    return set_error(nullptr, FFAI_ATTN_ERR_CUDA,
+                     "decode_static: a CUDA error was pending before the launch (left by "
+                     "earlier work on this thread): %s",
+                     cudaGetErrorString(e));
   e = launch_decode(p, static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return cuda_fail(nullptr, e, "launch_decode");
   return FFAI_ATTN_OK;
@@ -1585,11 +1618,14 @@ int ffai_gemm_bf16(ffai_attn_ctx* ctx, const void* a, int64_t lda, const void* b
   p.n_tiles = (N + 255) / 256;
   {
     // The last wave's tiles (fewer than the SMs) run as 128-column halves
-    // when that still fits one wave: the wave takes half as long.
+    // when that still fits one wave: the wave takes half as long.  Not when
+    // the right-most column of tiles is at most 128 columns wide: its second
+    // halves would lie wholly past N and take a CTA for no output.
     const long long tiles = static_cast<long long>(p.m_tiles) * p.n_tiles;
     const long long sms = ctx->num_sms;
     const long long tail = tiles - (tiles - 1) / sms * sms;  // tiles of the last wave
-    const bool split = 2 * tail <= sms;
+    const int last_cols = N - (p.n_tiles - 1) * 256;
+    const bool split = 2 * tail <= sms && last_cols > 128;
     p.split_from = static_cast<int>(split ? tiles - tail : tiles);
     p.items = static_cast<int>(split ? tiles + tail : tiles);
   }

@@ -168,7 +168,9 @@ int ffai_attn_decode(ffai_attn_ctx* ctx, const ffai_attn_desc* d, const void* q,
  * current; make that first call before any stream capture.  Calls that can
  * be in flight at the same time on one device (different streams or host
  * threads) share the scratch and race: serialise them.  Errors and declines
- * are reported through ffai_attn_last_error(NULL, ...). */
+ * are reported through ffai_attn_last_error(NULL, ...).  A CUDA error that
+ * earlier work left pending on the calling thread is reported as such
+ * (FFAI_ATTN_ERR_CUDA, nothing launched) and left in place for its owner. */
 int ffai_attn_decode_static(const ffai_attn_desc* d, const void* q, const void* k, const void* v,
                             void* o, float* lse, int32_t num_splits, void* stream);
 
@@ -397,7 +399,17 @@ int ffai_flash_serves(const ffai_tensor4* kt, const ffai_tensor4* v);
  * out (1,H,qlen,64) f32.  FFAI_ATTN_DECLINED where the reference returns
  * Ok(None): masked, head_dim != 64, keys below the floor
  * (FFAI_DECODE_MIN_KEYS for qlen = 1, 256 otherwise), qlen not in {1, keys},
- * or host memory. */
+ * or host memory.
+ *
+ * Numerics differ from the reference's f32 kernel at the encoder shape
+ * (qlen = keys): the f32 operands are rounded to bf16 on the device and run
+ * on the tensor cores with f32 accumulation, so the output differs from the
+ * reference's by about 5e-4 (max abs, Whisper-scaled inputs; the reference's
+ * own kernel matches its three-op path to 6.9e-7, flash_attn.rs:7).  With
+ * the environment variable FFAI_ATTN_CHECKED_F32=1 (read on every call) the
+ * encoder shape runs the f32 kernel instead, within 1e-5 relative of the
+ * reference, at a fraction of the throughput.  The decode shape (qlen = 1)
+ * always computes in f32 over the cache's own type. */
 int ffai_flash_attend(ffai_attn_ctx* ctx, const ffai_tensor4* q, const ffai_tensor4* kt,
                       const ffai_tensor4* v, int32_t masked, ffai_tensor4* out, void* stream);
 
@@ -405,6 +417,17 @@ int ffai_flash_attend(ffai_attn_ctx* ctx, const ffai_tensor4* q, const ffai_tens
  * encoder shape, writing out (1, seq, H*64) f32 directly. */
 int ffai_flash_attend_merged(ffai_attn_ctx* ctx, const ffai_tensor4* q, const ffai_tensor4* kt,
                              const ffai_tensor4* v, ffai_tensor4* out, void* stream);
+
+/* The decline decision of ffai_flash_attend (merged = 0) or
+ * ffai_flash_attend_merged (merged = 1) on the operands alone, without a
+ * context or a GPU: FFAI_ATTN_OK if the call would be served, else
+ * FFAI_ATTN_DECLINED (the reference's Ok(None)) or an error; the message is
+ * in ffai_attn_last_error(NULL, ...).  A candle op cannot return "declined"
+ * from its cuda_fwd, so the CUDA branch of attend / attend_merged asks here
+ * first, as the reference's functions check before apply_op3
+ * (flash_attn.rs:135-158, :218-264). */
+int ffai_flash_check(const ffai_tensor4* q, const ffai_tensor4* kt, const ffai_tensor4* v,
+                     int32_t masked, int32_t merged);
 
 #ifdef __cplusplus
 }

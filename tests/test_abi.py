@@ -89,6 +89,10 @@ def test_check_gate(lib):
     assert _check(lib, _abi.OP_DECODE, **{**dec, "q_len": 2}) == _abi.DECLINED
     assert _check(lib, _abi.OP_DECODE, **{**dec, "q_dtype": _abi.DT_F16}) == _abi.DECLINED
     assert _check(lib, _abi.OP_DECODE, **{**dec, "v_layout": _abi.LAYOUT_TOKEN_MAJOR}) == _abi.DECLINED
+    # the decode kernels read q and write out as dense rows: a fused-projection
+    # view (token_stride set) is declined rather than misread
+    assert _check(lib, _abi.OP_DECODE, **{**dec, "token_stride": 3 * 12 * 64}) == _abi.DECLINED
+    assert "token_stride" in _abi.last_error(None)
     # varlen
     tm = _abi.LAYOUT_TOKEN_MAJOR
     var = dict(heads=16, q_dtype=_abi.DT_BF16, kv_dtype=_abi.DT_BF16, q_layout=tm, k_layout=tm,
@@ -119,3 +123,34 @@ def test_serves_on_host_tensors_declines(lib):
     assert lib.ffai_flash_serves(ctypes.byref(kt), ctypes.byref(v)) == 1
     kt.dims[3] = v.dims[2] = 255  # below MIN_SEQ (flash_attn.rs:112-128)
     assert lib.ffai_flash_serves(ctypes.byref(kt), ctypes.byref(v)) == 0
+
+
+def test_flash_check_applies_the_reference_decline_rules(lib):
+    """ffai_flash_check: attend / attend_merged's decision on the operands
+    alone (flash_attn.rs:135-158, :218-264), without a context or a GPU."""
+    def t4(dims, dt=_abi.DT_F32, dev=0):
+        return _abi.Tensor4(None, (ctypes.c_int64 * 4)(*dims), dt, dev)
+
+    def check(q, kt, v, masked=0, merged=0):
+        return lib.ffai_flash_check(ctypes.byref(q), ctypes.byref(kt), ctypes.byref(v),
+                                    masked, merged)
+
+    enc = (t4((1, 6, 1500, 64)), t4((1, 6, 64, 1500)), t4((1, 6, 1500, 64)))
+    assert check(*enc) == _abi.OK
+    assert check(*enc, merged=1) == _abi.OK
+    assert check(*enc, masked=1) == _abi.DECLINED
+    # below MIN_SEQ at the encoder shape
+    short = (t4((1, 6, 200, 64)), t4((1, 6, 64, 200)), t4((1, 6, 200, 64)))
+    assert check(*short) == _abi.DECLINED
+    # decode shape: 16-bit caches are served, not at the encoder shape or merged
+    dec = (t4((1, 12, 1, 64)), t4((1, 12, 64, 1500), _abi.DT_F16), t4((1, 12, 1500, 64), _abi.DT_F16))
+    assert check(*dec) == _abi.OK
+    assert check(*dec, merged=1) == _abi.DECLINED
+    half_enc = (enc[0], t4((1, 6, 64, 1500), _abi.DT_BF16), t4((1, 6, 1500, 64), _abi.DT_BF16))
+    assert check(*half_enc) == _abi.DECLINED
+    # q_len neither 1 nor keys; host memory; mixed devices
+    mid = (t4((1, 6, 700, 64)), enc[1], enc[2])
+    assert check(*mid) == _abi.DECLINED
+    assert check(t4((1, 6, 1500, 64), dev=-1), *enc[1:]) == _abi.DECLINED
+    assert check(enc[0], t4((1, 6, 64, 1500), dev=1), enc[2]) == _abi.DECLINED
+    assert "device" in _abi.last_error(None)
