@@ -7,12 +7,21 @@ One step = one pass of encoder self-attention over this rank's share of the
 long-form workload (c4: 64 segments x 20 heads x 1500 frames x 64, bf16,
 scale 1/8; segments split contiguously over the N ranks, no collective on
 the data path).  `value` is whole-job TFLOP/s (4*B*H*N^2*d over the max
-over ranks of the CUDA-event time of K steps).  Extra keys: the roofline of
-the tensor-core kernel, the reference CPU kernel's rate on this host
-(cpu_baseline), an end-to-end number through the host-buffer C-ABI entry
-(e2e: host->device copies, kernels, device->host copies into one shared
-host output), decode-attention HBM GB/s (c3), and SM clocks sampled during
-the timed region.
+over ranks of the CUDA-event time of K steps).  The result line also holds
+the roofline of the tensor-core kernel, the reference CPU kernel's rate on
+this host (cpu_baseline), an end-to-end number through the host-buffer
+C-ABI entry (e2e: host->device copies, kernels, device->host copies into
+one shared host output), and SM clocks sampled during the timed region.
+
+The other configurations are measured after it and printed first, one short
+line each, `leg <name> {json}` (not JSON lines, so the result stays the one
+JSON line of the output, and it comes last): c1 (whisper-tiny, f32 through
+the reference-facing entry, the shape the reference publishes a number
+for), c2 (whisper-base batch), c3 (decode: cross-attention over 1500 keys,
+self-attention over {1, 32, 128, 448} keys, the paged cache), c5 (ragged
+packed segments, LPT over the ranks), each with its roofline fraction and
+the reference CPU kernel on this host beside it; then the projections and
+GEMVs around the attention.
 
 `--impl reference` times the reference's CPU kernel (the C++ restatement in
 oracle/, all host threads) on a bounded sample of the same workload.
@@ -81,6 +90,11 @@ class ClockSampler:
             self.nv = pynvml
             self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self.h, pynvml.NVML_CLOCK_SM)
             self.ok = True
+            # The first queries can stall the driver for a long time; take
+            # them here, outside any timed region, and drop the sample.
+            self._read()
+            self.samples.clear()
+            self.reasons = 0
         except Exception:
             pass
         self._stop = threading.Event()
@@ -108,6 +122,10 @@ class ClockSampler:
         if self.ok:
             self._t = threading.Thread(target=self._loop, daemon=True)
             self._t.start()
+            # the timed region starts once the sampler is running
+            t0 = time.perf_counter()
+            while not self.samples and time.perf_counter() - t0 < 5.0:
+                time.sleep(0.001)
 
     def stop(self):
         if self.ok and self._t:
@@ -144,6 +162,20 @@ def timed(dist, steps, fn):
     return dist.max(local), local
 
 
+# ----------------------------------------------------------------- config
+def job_config(cfg, world: int) -> dict:
+    """The headline workload's `config`, identical in both arms."""
+    from ffai_b200 import partition, workloads
+    lo, hi = partition.contiguous_ranges(cfg.segments, world)[0]
+    shard_in = 3 * (hi - lo) * cfg.heads * cfg.seq * 64 * 2
+    copies = max(1, math.ceil(2 * L2_BYTES / max(shard_in, 1)))
+    return {"workload": cfg.name, "segments": cfg.segments, "heads": cfg.heads,
+            "seq_len": cfg.seq, "head_dim": 64, "causal": False, "scale": workloads.SCALE,
+            "out_dtype": "bf16",
+            "partition": f"contiguous over {world} rank(s), no collective",
+            "l2": f"inputs > L2 ({copies} x {shard_in / 2**20:.0f} MB/rank)"}
+
+
 # ----------------------------------------------------------------- CPU baseline
 def cpu_encoder_rate(cfg, budget_s: float, seed: int = 0, max_segments: int | None = None):
     """The reference CPU kernel (oracle restatement, AVX2, all host threads)
@@ -173,8 +205,7 @@ def cpu_encoder_rate(cfg, budget_s: float, seed: int = 0, max_segments: int | No
     for _ in range(runs):
         oracle.flash_units(qn, ktn, vn, threads=threads)
     dt = time.perf_counter() - t0
-    sample = (f"{nseg} segment(s) x {cfg.heads} heads x {cfg.seq}^2 of {cfg.name} "
-              f"(bf16-rounded, widened to f32), {runs} run(s), {dt:.1f} s")
+    sample = f"{nseg} segment(s) of {cfg.name}, f32 on bf16-rounded values, {runs} run(s), {dt:.1f} s"
     return flops * runs / dt / 1e12, threads, sample, dt / runs, (qn, ktn, vn, flops, threads)
 
 
@@ -207,10 +238,8 @@ def run_reference(args, dist):
         "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": round(total / args.steps * 1e3, 3), "higher_is_better": True,
         "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": cfg.name, "segments": cfg.segments, "heads": cfg.heads,
-                   "seq_len": cfg.seq, "head_dim": 64, "scale": workloads.SCALE,
-                   "implementation": "C++ AVX2 restatement of flash_attn.rs (oracle/), "
-                                     "the Rust reference has no toolchain here"},
+        "config": job_config(cfg, args.gpus),
+        "implementation": "C++ AVX2 restatement of flash_attn.rs (oracle/); no Rust toolchain here",
         "cpu_baseline": {"value": round(value, 4), "unit": "TFLOP/s", "cores": threads,
                          "kind": "port", "sample": sample},
         "e2e": {"value": round(value, 4), "unit": "TFLOP/s", "h2d_bytes_per_step": 0,
@@ -219,67 +248,208 @@ def run_reference(args, dist):
     print(json.dumps(line), flush=True)
 
 
+# ----------------------------------------------------------------- legs
+def leg_line(name: str, d: dict) -> str:
+    """One measured configuration as a short line: `leg <name> {json}`."""
+    return f"leg {name} " + json.dumps(d, separators=(",", ":"))
+
+
+def event_seconds(fn, reps: int, warm: int = 3) -> float:
+    """Seconds per call of fn(): CUDA events on the current stream around
+    `reps` calls, after `warm` untimed ones, synchronized on both sides."""
+    import torch
+    for _ in range(warm):
+        fn()
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(reps):
+        fn()
+    b.record()
+    torch.cuda.synchronize()
+    return a.elapsed_time(b) / 1e3 / reps
+
+
+def graph_seconds(calls, reps: int) -> float:
+    """Seconds per call, the calls captured in one CUDA graph and replayed
+    `reps` times (a Python call costs more than a launch of a decode or GEMV
+    kernel)."""
+    import torch
+    for c in calls:
+        c()
+    torch.cuda.synchronize()
+    gr = torch.cuda.CUDAGraph()
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        for c in calls:
+            c()
+        torch.cuda.synchronize()
+        with torch.cuda.graph(gr, stream=s):
+            for c in calls:
+                c()
+    torch.cuda.current_stream().wait_stream(s)
+    for _ in range(3):
+        gr.replay()
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(reps):
+        gr.replay()
+    b.record()
+    torch.cuda.synchronize()
+    del gr
+    return a.elapsed_time(b) / 1e3 / (reps * len(calls))
+
+
+def repeat_seconds(fn, budget_s: float) -> tuple[float, int]:
+    """Host wall time per call of fn() over about `budget_s` seconds."""
+    fn()
+    runs, t0 = 0, time.perf_counter()
+    while time.perf_counter() - t0 < budget_s or runs == 0:
+        fn()
+        runs += 1
+    return (time.perf_counter() - t0) / runs, runs
+
+
+# ----------------------------------------------------------------- c1, c2
+def bench_c1(steps: int, dev, peaks, cpu_budget: float):
+    """c1, the shape the reference publishes its number on (flash_attn.rs:6):
+    1 x 6 heads x 1500 x 64, f32 operands, q pre-scaled, K given as K^T,
+    f32 output, through the reference-facing entry ffai_flash_attend (f32
+    operands rounded to bf16 on the device, tensor-core kernel) and in the
+    checked-f32 mode; beside it the reference CPU kernel (oracle restatement)
+    on 1 and on all host threads."""
+    import numpy as np
+    import torch
+
+    from ffai_b200 import attention, flash_attn, workloads
+    from oracle import oracle
+    cfg = workloads.C1
+    q, k, v = workloads.encoder_inputs(cfg, seed=0, device=dev)
+    qs = (q * workloads.SCALE).contiguous()
+    kt = k.transpose(-1, -2).contiguous()
+    reps = max(10, steps)
+    t_drop = event_seconds(lambda: flash_attn.attend(qs, kt, v, False), reps)
+    qb, kb, vb = (t.to(torch.bfloat16) for t in (q, k, v))
+    ob = torch.empty(q.shape, dtype=torch.float32, device=dev)
+    t_kern = event_seconds(lambda: attention.prefill(qb, kb, vb, scale=workloads.SCALE, out=ob), reps)
+    of = torch.empty(q.shape, dtype=torch.float32, device=dev)
+    t_chk = event_seconds(lambda: attention.prefill(q, k, v, scale=workloads.SCALE, checked=True,
+                                                    out=of), max(3, reps // 4))
+    flops = cfg.flops
+    res = {"workload": "c1 1x6x1500^2 f32",
+           "dropin_tflops": round(flops / t_drop / 1e12, 2), "dropin_us": round(t_drop * 1e6, 1),
+           "kernel_tflops": round(flops / t_kern / 1e12, 2),
+           "kernel_frac": round(flops / t_kern / 1e12 / peaks["bf16_tflops"], 4),
+           "checked_f32_tflops": round(flops / t_chk / 1e12, 3)}
+    if cpu_budget > 0:
+        oracle.build()
+        U = cfg.heads
+        qn = qs.cpu().numpy().reshape(U, cfg.seq, 64)
+        ktn = np.ascontiguousarray(kt.cpu().numpy().reshape(U, 64, cfg.seq))
+        vn = np.ascontiguousarray(v.cpu().numpy().reshape(U, cfg.seq, 64))
+        threads = os.cpu_count() or 1
+        t_n, runs_n = repeat_seconds(lambda: oracle.flash_units(qn, ktn, vn, threads=threads),
+                                     cpu_budget)
+        t_1, runs_1 = repeat_seconds(lambda: oracle.flash_units(qn[:1], ktn[:1], vn[:1], threads=1),
+                                     cpu_budget / 2)
+        res["cpu"] = {"kind": "port", "gflops_nt": round(flops / t_n / 1e9, 1), "cores": threads,
+                      "gflops_1t": round(flops / U / t_1 / 1e9, 1)}
+        res["ref_published_gflops"] = 331
+    return res
+
+
+def bench_c2(steps: int, dev, peaks, cpu_budget: float):
+    """c2: 8 segments x 8 heads x 1500 x 64, bf16, through ffai_attn_prefill
+    (bf16 output); the reference CPU kernel on a one-segment sample."""
+    import torch
+
+    from ffai_b200 import attention, workloads
+    cfg = workloads.C2
+    q, k, v = workloads.encoder_inputs(cfg, seed=0, device=dev)
+    o = torch.empty_like(q)
+    t = event_seconds(lambda: attention.prefill(q, k, v, scale=workloads.SCALE, out=o),
+                      max(10, steps))
+    res = {"workload": "c2 8x8x1500^2 bf16",
+           "tflops": round(cfg.flops / t / 1e12, 2), "us": round(t * 1e6, 1),
+           "frac": round(cfg.flops / t / 1e12 / peaks["bf16_tflops"], 4)}
+    if cpu_budget > 0:
+        rate, threads, _, _, _ = cpu_encoder_rate(cfg, budget_s=cpu_budget, max_segments=1)
+        res["cpu"] = {"kind": "port", "tflops_nt": round(rate, 4), "cores": threads}
+    return res
+
+
 # ----------------------------------------------------------------- decode (c3)
-def bench_decode(steps: int):
-    """Decode attention HBM GB/s on the c3 shapes over distinct per-layer caches
-    (more bytes than L2 per pass), plain launches and one CUDA graph."""
+def cpu_decode_rate(keys: int, budget_s: float):
+    """The reference's 16-bit-cache decode kernel (xattn_head_f16,
+    flash_attn.rs:714-789, oracle restatement) on the c3 cross-attention
+    shape: 60 rows (5 beams x 12 heads) over an f16 cache, on 1 and on all
+    host threads.  Returns GB/s of the same algorithmic bytes as the GPU leg."""
+    import numpy as np
+
+    from oracle import oracle
+    oracle.build()
+    rng = np.random.default_rng(21)
+    rows = 60
+    q = (rng.standard_normal((rows, 64), dtype=np.float32) * np.float32(0.5)).astype(np.float32)
+    kt = rng.standard_normal((rows, 64, keys), dtype=np.float32).astype(np.float16).view(np.uint16)
+    vv = rng.standard_normal((rows, keys, 64), dtype=np.float32).astype(np.float16).view(np.uint16)
+    nbytes = rows * (2 * keys * 64 * 2) + rows * 64 * 8
+    threads = os.cpu_count() or 1
+    t1, _ = repeat_seconds(lambda: oracle.xattn_rows_f16(q, kt, vv, threads=1), budget_s / 2)
+    tn, _ = repeat_seconds(lambda: oracle.xattn_rows_f16(q, kt, vv, threads=threads), budget_s / 2)
+    return {"kind": "port", "gbs_1t": round(nbytes / t1 / 1e9, 2),
+            "gbs_nt": round(nbytes / tn / 1e9, 2), "cores": threads}
+
+
+def bench_decode(steps: int, peaks, cpu_budget: float):
+    """Decode attention HBM GB/s on the c3 shapes (5 beams x 12 heads, bf16
+    cache, q f32): cross-attention over 1500 keys and self-attention over
+    {1, 32, 128, 448} keys, each over distinct per-layer caches (a Whisper
+    step visits every layer's cache once, between them the projections'
+    weights stream through L2), in a CUDA graph; plus the paged cache."""
     import torch
 
     from ffai_b200 import attention, workloads
     dev = torch.device("cuda", torch.cuda.current_device())
-    res = {}
+    rows = workloads.C3_BEAMS * workloads.C3_HEADS
+    legs = {}
     # Cross-attention caches are written once per utterance (kv_stable: the
     # kernel may copy them before the preceding kernel finishes); the
     # self-attention cache gets its newest key from the preceding kernel.
-    for name, keys, layers, stable in (("cross_1500", workloads.C3_CROSS_KEYS, 12, True),
-                                       ("self_448", 448, 24, False)):
+    cases = [("cross", workloads.C3_CROSS_KEYS, True)] + [
+        ("self", n, False) for n in workloads.C3_SELF_KEYS]
+    for kind, keys, stable in cases:
+        bytes_per = rows * (2 * keys * 64 * 2) + rows * 64 * (4 + 4)
+        layers = min(256, max(24, math.ceil(2 * L2_BYTES / bytes_per)))
         caches = [workloads.decode_inputs(keys, seed=100 + l, device=dev) for l in range(layers)]
         outs = [torch.empty(5, 12, 1, 64, device=dev) for _ in range(layers)]
-        rows = workloads.C3_BEAMS * workloads.C3_HEADS
-        bytes_per = rows * (2 * keys * 64 * 2) + rows * 64 * (4 + 4)
-
-        def one_pass():
-            for (q, k, v), o in zip(caches, outs):
-                attention.decode(q, k, v, out=o, kv_stable=stable)
-
-        for _ in range(3):
-            one_pass()
-        torch.cuda.synchronize()
-        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        a.record()
-        for _ in range(steps):
-            one_pass()
-        b.record()
-        torch.cuda.synchronize()
-        t_launch = a.elapsed_time(b) / 1e3 / (steps * layers)
-        g = torch.cuda.CUDAGraph()
-        s = torch.cuda.Stream()
-        s.wait_stream(torch.cuda.current_stream())
-        with torch.cuda.stream(s):
-            one_pass()
-            torch.cuda.synchronize()
-            with torch.cuda.graph(g, stream=s):
-                one_pass()
-        torch.cuda.current_stream().wait_stream(s)
-        for _ in range(3):
-            g.replay()
-        torch.cuda.synchronize()
-        a.record()
-        for _ in range(steps):
-            g.replay()
-        b.record()
-        torch.cuda.synchronize()
-        t_graph = a.elapsed_time(b) / 1e3 / (steps * layers)
-        del g
-        res[name] = {"rows": rows, "keys": keys, "layers_per_pass": layers, "kv_stable": stable,
-                     "kernel": "decode_cluster_kernel",
-                     "bytes_per_launch": bytes_per,
-                     "us_per_launch": round(t_launch * 1e6, 2),
-                     "gbs": round(bytes_per / t_launch / 1e9, 1),
-                     "us_per_launch_graph": round(t_graph * 1e6, 2),
-                     "gbs_graph": round(bytes_per / t_graph / 1e9, 1)}
-    res["self_448_paged"] = bench_decode_paged(steps, dev)
-    return res
+        calls = [lambda c=c, o=o: attention.decode(c[0], c[1], c[2], out=o, kv_stable=stable)
+                 for c, o in zip(caches, outs)]
+        t = graph_seconds(calls, max(5, min(steps, 50)))
+        r = {"rows": rows, "us": round(t * 1e6, 2), "gbs": round(bytes_per / t / 1e9, 1),
+             "frac": round(bytes_per / t / 1e9 / peaks["hbm_gbs"], 4)}
+        in_l2 = layers * bytes_per <= L2_BYTES
+        if kind == "cross":
+            def one_pass():
+                for c in calls:
+                    c()
+            r["us_plain"] = round(event_seconds(one_pass, max(5, min(steps, 50))) / layers * 1e6, 2)
+            if cpu_budget > 0:
+                r["cpu"] = cpu_decode_rate(keys, cpu_budget)
+            legs["c3_cross_1500"] = r
+        else:
+            sl = legs.setdefault("c3_self", {"rows": rows})
+            sl[str(keys)] = [r["us"], r["gbs"], r["frac"]]
+            if in_l2:
+                sl.setdefault("in_l2", []).append(keys)
+        del caches, outs, calls
+    legs["c3_self"]["cols"] = "us, GB/s, frac"
+    p = bench_decode_paged(steps, dev)
+    p["frac"] = round(p["gbs"] / peaks["hbm_gbs"], 4)
+    legs["c3_paged_448"] = p
+    return legs
 
 
 def bench_decode_paged(steps: int, dev):
@@ -300,39 +470,14 @@ def bench_decode_paged(steps: int, dev):
     lens = torch.full((beams,), keys, dtype=torch.int32, device=dev)
     q = torch.randn(beams, heads, 1, 64, device=dev) * 0.5
     outs = [torch.empty(beams, heads, 1, 64, device=dev) for _ in range(layers)]
-
-    def one_pass():
-        for (kp, vp), tb, o in zip(pools, tables, outs):
-            kvcache.decode_paged(q, kp, vp, tb, lens, out=o, kv_bound=keys)
-
-    for _ in range(3):
-        one_pass()
-    torch.cuda.synchronize()
-    gr = torch.cuda.CUDAGraph()
-    s = torch.cuda.Stream()
-    s.wait_stream(torch.cuda.current_stream())
-    with torch.cuda.stream(s):
-        one_pass()
-        torch.cuda.synchronize()
-        with torch.cuda.graph(gr, stream=s):
-            one_pass()
-    torch.cuda.current_stream().wait_stream(s)
-    for _ in range(3):
-        gr.replay()
-    torch.cuda.synchronize()
-    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    a.record()
-    for _ in range(steps):
-        gr.replay()
-    b.record()
-    torch.cuda.synchronize()
-    t = a.elapsed_time(b) / 1e3 / (steps * layers)
-    del gr
+    calls = [lambda kp=kp, vp=vp, tb=tb, o=o: kvcache.decode_paged(q, kp, vp, tb, lens, out=o,
+                                                                  kv_bound=keys)
+             for (kp, vp), tb, o in zip(pools, tables, outs)]
+    t = graph_seconds(calls, max(5, min(steps, 50)))
     rows = beams * heads
     bytes_per = rows * (2 * keys * 64 * 2) + rows * 64 * (4 + 4)
-    return {"rows": rows, "keys": keys, "layers_per_pass": layers, "page_keys": 64,
-            "kernel": "decode_cluster_kernel (paged)", "bytes_per_launch": bytes_per,
-            "us_per_launch_graph": round(t * 1e6, 2), "gbs_graph": round(bytes_per / t / 1e9, 1)}
+    return {"rows": rows, "keys": keys, "page_keys": 64, "us": round(t * 1e6, 2),
+            "gbs": round(bytes_per / t / 1e9, 1)}
 
 
 def bench_int8_gemv(steps: int, dev):
@@ -353,41 +498,12 @@ def bench_int8_gemv(steps: int, dev):
         nb = q.cols // q.blk
         return q.rows * (q.cols + 4 * nb + 4) + batch * 4 * (q.cols + q.rows)
 
-    def time_calls(calls, reps):
-        """Seconds per call, the calls captured in one CUDA graph (a Python
-        call costs more than a launch of these kernels)."""
-        for c in calls:
-            c()
-        torch.cuda.synchronize()
-        gr = torch.cuda.CUDAGraph()
-        s = torch.cuda.Stream()
-        s.wait_stream(torch.cuda.current_stream())
-        with torch.cuda.stream(s):
-            for c in calls:
-                c()
-            torch.cuda.synchronize()
-            with torch.cuda.graph(gr, stream=s):
-                for c in calls:
-                    c()
-        torch.cuda.current_stream().wait_stream(s)
-        for _ in range(3):
-            gr.replay()
-        torch.cuda.synchronize()
-        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        a.record()
-        for _ in range(reps):
-            gr.replay()
-        b.record()
-        torch.cuda.synchronize()
-        del gr
-        return a.elapsed_time(b) / 1e3 / (reps * len(calls))
-
     vocab = [Int8Gemv.new(torch.randn(51865, 1280, device=dev, generator=g) * 0.05)
              for _ in range(3)]
     for batch in (1, 5):
         x = torch.randn(batch, 1280, device=dev, generator=g)
         outs = [torch.empty(batch, 51865, device=dev) for _ in vocab]
-        t = time_calls([lambda q=q, o=o: q.forward(x, out=o) for q, o in zip(vocab, outs)],
+        t = graph_seconds([lambda q=q, o=o: q.forward(x, out=o) for q, o in zip(vocab, outs)],
                        max(4, steps))
         nbytes = algo_bytes(vocab[0], batch)
         res[f"vocab_51865x1280_b{batch}"] = {
@@ -405,7 +521,7 @@ def bench_int8_gemv(steps: int, dev):
     calls = []
     for a1, a2 in zip(fc1, fc2):
         calls += [lambda q=a1: q.forward(x1, out=o1), lambda q=a2: q.forward(x2, out=o2)]
-    t = time_calls(calls, max(2, steps // 2))
+    t = graph_seconds(calls, max(2, steps // 2))
     nbytes = (algo_bytes(fc1[0], 5) + algo_bytes(fc2[0], 5)) / 2
     res["mlp_fc1_fc2_b5"] = {"kernel": "int8_gemv_kernel", "layers": layers,
                              "bytes_per_launch": int(nbytes), "us_per_launch": round(t * 1e6, 2),
@@ -446,33 +562,6 @@ def bench_f16_gemv(steps: int, dev):
     res = {}
     g = torch.Generator(device=dev).manual_seed(13)
 
-    def graph_time(calls, reps):
-        for c in calls:
-            c()
-        torch.cuda.synchronize()
-        gr = torch.cuda.CUDAGraph()
-        s = torch.cuda.Stream()
-        s.wait_stream(torch.cuda.current_stream())
-        with torch.cuda.stream(s):
-            for c in calls:
-                c()
-            torch.cuda.synchronize()
-            with torch.cuda.graph(gr, stream=s):
-                for c in calls:
-                    c()
-        torch.cuda.current_stream().wait_stream(s)
-        for _ in range(3):
-            gr.replay()
-        torch.cuda.synchronize()
-        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        a.record()
-        for _ in range(reps):
-            gr.replay()
-        b.record()
-        torch.cuda.synchronize()
-        del gr
-        return a.elapsed_time(b) / 1e3 / (reps * len(calls))
-
     layer = (("qkv_3840x1280", 3840, 1280), ("o_1280x1280", 1280, 1280),
              ("fc1_5120x1280", 5120, 1280), ("fc2_1280x5120", 1280, 5120))
     for name, rows, cols, copies in [(n, r, c, 32) for n, r, c in layer] + [
@@ -482,7 +571,7 @@ def bench_f16_gemv(steps: int, dev):
         for batch in (1, 5):
             x = torch.randn(batch, cols, device=dev, generator=g)
             outs = [torch.empty(batch, rows, device=dev) for _ in qs]
-            t = graph_time([lambda q=q, o=o: q.forward(x, out=o) for q, o in zip(qs, outs)],
+            t = graph_seconds([lambda q=q, o=o: q.forward(x, out=o) for q, o in zip(qs, outs)],
                            max(2, steps // 4))
             nbytes = rows * cols * 2 + 4 * rows + batch * 4 * (cols + rows)
             res[f"{name}_b{batch}"] = {"kernel": "f16_gemv_kernel", "bytes_per_launch": nbytes,
@@ -557,12 +646,14 @@ def bench_projections(steps: int, dev):
     return res
 
 
-def bench_ragged(dist, steps: int, peaks):
+def bench_ragged(dist, steps: int, peaks, cpu_budget: float):
     """c5: 256 packed segments of U{200..1500} frames, 16 heads, through the
     varlen entry; segments assigned to ranks longest-processing-time first on
     L^2.  Device time max over ranks; plus an end-to-end figure through the
     public API with pinned host buffers (H2D of the packed q/k/v, D2H of the
-    output inside the timed region)."""
+    output inside the timed region), and on rank 0 of a 1-rank run the
+    reference CPU kernel on a sample of the segments."""
+    import numpy as np
     import torch
 
     from ffai_b200 import attention, partition, workloads
@@ -595,19 +686,37 @@ def bench_ragged(dist, steps: int, peaks):
     e_max, _ = timed(dist, e_steps, e2e_step)
     ok = bool(torch.equal(hout, out.cpu()))
     oks = dist.gather_objects(ok)
-    achieved = flops_rank / (t_local / steps) / 1e12
-    return {"workload": "whisper-medium-ragged-c5", "segments": len(lengths), "heads": 16,
-            "total_tokens": int(sum(lengths)), "exact_flops": flops_job,
-            "tflops": round(flops_job * steps / t_max / 1e12, 2),
-            "ms_per_step": round(t_max / steps * 1e3, 4),
-            "frac_of_peak_rank0": round(achieved / peaks["bf16_tflops"], 4),
-            "assignment": "LPT on L^2 per rank",
-            "rank_load_imbalance": round(max(load) / (sum(load) / len(load)), 4),
-            "rank_tokens": tokens,
-            "e2e_tflops": round(flops_job * e_steps / e_max / 1e12, 3),
-            "e2e_h2d_bytes_per_step": int(3 * sum(lengths) * 16 * 64 * 2),
-            "e2e_d2h_bytes_per_step": int(sum(lengths) * 16 * 64 * 2),
-            "e2e_matches_device": all(oks)}
+    fracs = dist.gather_objects(flops_rank / (t_local / steps) / 1e12 / peaks["bf16_tflops"])
+    res = {"workload": "c5 ragged 256 seg x16 heads bf16",
+           "tflops": round(flops_job * steps / t_max / 1e12, 2),
+           "ms": round(t_max / steps * 1e3, 4), "n_gpus": dist.world,
+           "frac_min_rank": round(min(fracs), 4),
+           "imbalance": round(max(load) / (sum(load) / len(load)), 4),
+           "e2e_tflops": round(flops_job * e_steps / e_max / 1e12, 3), "e2e_ok": all(oks)}
+    if cpu_budget > 0 and dist.world == 1:
+        from oracle import oracle
+        oracle.build()
+        threads = os.cpu_count() or 1
+        # the segments nearest the mean length, as many as keep every thread busy
+        mean = sum(lengths) / len(lengths)
+        pick = sorted(range(len(lengths)), key=lambda s: abs(lengths[s] - mean))[:max(1, threads // 16)]
+        units, fl = [], 0.0
+        for s in pick:
+            L = lengths[s]
+            a_, b_ = cu[s], cu[s + 1]
+            qs = (q[a_:b_].float() * workloads.SCALE).permute(1, 0, 2).contiguous().cpu().numpy()
+            kt = k[a_:b_].float().permute(1, 2, 0).contiguous().cpu().numpy()
+            vs = v[a_:b_].float().permute(1, 0, 2).contiguous().cpu().numpy()
+            units.append((qs, kt, vs))
+            fl += workloads.ragged_flops([L])
+
+        def run():
+            for qs, kt, vs in units:
+                oracle.flash_units(qs, kt, vs, threads=threads)
+
+        tc, runs = repeat_seconds(run, cpu_budget)
+        res["cpu"] = {"kind": "port", "tflops_nt": round(fl / tc / 1e12, 4), "cores": threads}
+    return res
 
 
 # ----------------------------------------------------------------- our arm
@@ -676,10 +785,9 @@ def run_ours(args, dist):
     roofline = {"bound": "tensor", "achieved": round(achieved, 2), "peak": peaks["bf16_tflops"],
                 "unit": "TFLOP/s", "frac": round(achieved / peaks["bf16_tflops"], 4),
                 "traffic": (int(tr * nseg) if tr else None),
-                "peak_source": f"{peaks['source']} bf16 burst (cuBLAS)",
-                "kernel": "prefill_tc_kernel", "kernel_ms_avg": round(k_avg * 1e3, 4),
-                "algorithmic_flops_per_launch": flops_rank,
-                "algorithmic_bytes_per_launch": int(4 * nseg * seg_bytes)}
+                "peak_source": f"{peaks['source']} burst",
+                "kernel": "prefill_tc_kernel", "kernel_ms": round(k_avg * 1e3, 4),
+                "flops_per_launch": flops_rank}
 
     # --- end to end through the host-buffer C-ABI entry, host gather
     e2e = None
@@ -717,45 +825,53 @@ def run_ours(args, dist):
                "h2d_bytes_per_step": int(3 * cfg.segments * seg_bytes),
                "d2h_bytes_per_step": int(out_bytes),
                "ms_per_step": round(e_max / e_steps * 1e3, 3),
-               "entry": "ffai_attn_prefill_host (host buffers, pinned)",
-               "host_gather": ("shared /dev/shm buffer, pinned" if dist.world > 1 and pinned
-                               else "shared /dev/shm buffer, pageable" if dist.world > 1
-                               else "pinned host buffer"),
-               "gather_checksum_ok": gather_ok}
+               "entry": "ffai_attn_prefill_host",
+               "gather": ("/dev/shm, pinned" if dist.world > 1 and pinned
+                          else "/dev/shm, pageable" if dist.world > 1 else "pinned"),
+               "gather_ok": gather_ok}
         dist.barrier()
         if shared is not None:
             del raw, host_out
             shared.close(unlink=dist.rank == 0)
 
-    ragged = None
+    legs = []  # (name, dict), printed before the result line, the most looked-at last
+    cpu_budget = 0.0 if args.no_cpu_baseline else args.leg_cpu_seconds
+    cur = torch.device("cuda", torch.cuda.current_device())
+    # Per-GPU legs run in 1-GPU runs only; a multi-GPU run adds c5 on all ranks.
+    single = dist.world == 1
+    if single and not args.no_legs:
+        legs.append(("c1", bench_c1(args.steps, cur, peaks, cpu_budget)))
+        legs.append(("c2", bench_c2(args.steps, cur, peaks, cpu_budget)))
+    dec = {}
+    if single and not args.no_decode:
+        dec = bench_decode(args.steps, peaks, cpu_budget)
+        legs += [(n, dec.pop(n)) for n in ("c3_self", "c3_paged_448")]
     if not args.no_ragged:
-        ragged = bench_ragged(dist, max(5, min(args.steps, 20)), peaks)
-
-    decode = None
-    if dist.rank == 0 and not args.no_decode:
-        decode = bench_decode(max(5, min(args.steps, 50)))
-        for v_ in decode.values():
-            v_["frac_of_hbm"] = round(v_["gbs_graph"] / peaks["hbm_gbs"], 4)
-
-    proj = None
-    if dist.rank == 0 and not args.no_gemm:
-        proj = bench_projections(max(5, min(args.steps, 20)), torch.device("cuda", torch.cuda.current_device()))
-        for v_ in proj.values():
-            v_["frac_of_peak"] = round(v_["tflops"] / peaks["bf16_tflops"], 4)
-
-    f16 = None
-    if dist.rank == 0 and not args.no_f16:
-        f16 = bench_f16_gemv(max(5, min(args.steps, 50)), torch.device("cuda", torch.cuda.current_device()))
-        for k_, v_ in f16.items():
-            if isinstance(v_, dict) and not k_.startswith("cpu"):
-                v_["frac_of_hbm"] = round(v_["gbs"] / peaks["hbm_gbs"], 4)
-
-    int8 = None
-    if dist.rank == 0 and not args.no_int8:
-        int8 = bench_int8_gemv(max(5, min(args.steps, 50)), torch.device("cuda", torch.cuda.current_device()))
-        for k_, v_ in int8.items():
-            if not k_.startswith("cpu"):
-                v_["frac_of_hbm"] = round(v_["gbs"] / peaks["hbm_gbs"], 4)
+        legs.append(("c5", bench_ragged(dist, max(5, min(args.steps, 20)), peaks,
+                                        cpu_budget if single else 0.0)))
+    legs += list(dec.items())
+    fleg = []  # the projections and GEMVs around the attention, printed first
+    if single and not args.no_gemm:
+        proj = bench_projections(max(5, min(args.steps, 20)), cur)
+        fleg.append(("f_gemm", {k_: [v_["tflops"], round(v_["tflops"] / peaks["bf16_tflops"], 3),
+                                     v_["torch_linear_tflops"]] for k_, v_ in proj.items()}
+                     | {"cols": "tflops, frac, torch linear tflops", "m": 24000}))
+    if single and not args.no_f16:
+        f16 = bench_f16_gemv(max(5, min(args.steps, 50)), cur)
+        cpu16 = f16.pop("cpu_fc1_5120x1280_b1")
+        lay = f16.pop("decoder_layer_projections_b5_us")
+        fleg.append(("f_f16_gemv", {k_: [v_["us_per_launch"], v_["gbs"],
+                                         round(v_["gbs"] / peaks["hbm_gbs"], 3)]
+                                    for k_, v_ in f16.items()}
+                     | {"cols": "us, GB/s, frac", "layer_b5_us": lay,
+                        "cpu_fc1_b1_us": cpu16["us_per_call"]}))
+    if single and not args.no_int8:
+        i8 = bench_int8_gemv(max(5, min(args.steps, 50)), cur)
+        cpu8 = i8.pop("cpu_vocab_51865x1280_b1")
+        fleg.append(("f_int8_gemv", {k_: [v_["us_per_launch"], v_["gbs"],
+                                          round(v_["gbs"] / peaks["hbm_gbs"], 3)]
+                                     for k_, v_ in i8.items()}
+                     | {"cols": "us, GB/s, frac", "cpu_vocab_b1_us": cpu8["us_per_call"]}))
 
     cpu = None
     if dist.rank == 0 and dist.world == 1 and not args.no_cpu_baseline:
@@ -763,42 +879,29 @@ def run_ours(args, dist):
         # One thread on one head, as a per-core figure beside the all-threads one.
         from oracle import oracle
         qn, ktn, vn, _, _ = data
-        t0 = time.perf_counter()
-        runs1 = 0
-        while time.perf_counter() - t0 < 2.0 or runs1 == 0:
-            oracle.flash_units(qn[:1], ktn[:1], vn[:1], threads=1)
-            runs1 += 1
-        rate1 = 4.0 * cfg.seq * cfg.seq * 64 * runs1 / (time.perf_counter() - t0) / 1e12
+        t1, runs1 = repeat_seconds(lambda: oracle.flash_units(qn[:1], ktn[:1], vn[:1], threads=1),
+                                   2.0)
         cpu = {"value": round(rate, 4), "unit": "TFLOP/s", "cores": threads, "kind": "port",
-               "sample": sample, "value_1_thread": round(rate1, 5),
-               "sample_1_thread": f"1 head x {cfg.seq}^2, {runs1} run(s), 1 thread"}
+               "sample": sample, "value_1_thread": round(4.0 * cfg.seq * cfg.seq * 64 / t1 / 1e12, 5)}
 
     if dist.rank == 0:
+        conf = job_config(cfg, dist.world)
         line = {
             "metric": METRIC, "value": round(value, 2), "unit": "TFLOP/s",
             "n_gpus": dist.world, "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": round(t_max / args.steps * 1e3, 4), "higher_is_better": True,
             "scaling": "strong", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-            "config": {"workload": cfg.name, "segments": cfg.segments, "heads": cfg.heads,
-                       "seq_len": cfg.seq, "head_dim": 64, "causal": False,
-                       "scale": workloads.SCALE, "out_dtype": "bf16",
-                       "partition": f"{cfg.segments} segments split contiguously over "
-                                    f"{dist.world} rank(s), no data-path collective",
-                       "l2": f"inputs larger than L2: {copies} rotating cop(ies) of "
-                             f"{shard_in / 2**20:.0f} MB per rank"},
+            "config": conf,
             "segments_per_s": round(cfg.segments * args.steps / t_max, 1),
             "roofline": roofline,
             "cpu_baseline": cpu,
             "e2e": e2e,
             "gpu_launches": int(n_launch),
             "clocks": clocks.summary(),
-            "decode": decode,
-            "ragged_c5": ragged,
-            "int8_gemv": int8,
-            "f16_gemv": f16,
-            "encoder_projections": proj,
         }
-        print(json.dumps(line), flush=True)
+        for name, d in fleg + legs:
+            print(leg_line(name, d), flush=True)
+        print(json.dumps(line, separators=(",", ":")), flush=True)
     dist.barrier()
     dist.close()
 
@@ -816,7 +919,10 @@ def main():
     ap.add_argument("--no-f16", action="store_true")
     ap.add_argument("--no-gemm", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-legs", action="store_true", help="skip the c1 and c2 legs")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    ap.add_argument("--leg-cpu-seconds", type=float, default=3.0,
+                    help="host seconds for each leg's CPU baseline (0: none)")
     ap.add_argument("--segments", type=int, default=0,
                     help="profiling only: run a smaller batch of c4 segments")
     args = ap.parse_args()
