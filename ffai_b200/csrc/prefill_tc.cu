@@ -143,32 +143,32 @@ __device__ __forceinline__ void run_producer(const CUtensorMap* tmQ, const CUten
     const int ks = __ldg(p.k_start + w.seq);
     for (int t = 0; ok && t < w.ntiles; ++t) {
       if (q_use[t] > 0 &&
-          !mbar_wait(&bars->q_empty[t], (q_use[t] - 1) & 1, abort_flag, p.err, kErrTimeoutProducer)) {
+          !warp_wait(&bars->q_empty[t], (q_use[t] - 1) & 1, abort_flag, p.err, kErrTimeoutProducer)) {
         ok = false;
         break;
       }
       int c1, c2;
       box_coords(p.q_token_major, qs, p.heads, w.seq, w.head, w.row0 + t * kTcRows, c1, c2);
-      mbar_arrive_expect_tx(&bars->q_full[t], kTileBytes);
-      tma_load_3d(sQ + t * kTileBytes, tmQ, &bars->q_full[t], 0, c1, c2);
+      mbar_arrive_expect_tx_w(&bars->q_full[t], kTileBytes);
+      tma_load_3d_w(sQ + t * kTileBytes, tmQ, &bars->q_full[t], 0, c1, c2);
       ++q_use[t];
     }
     const int nblk = unit_blocks(p, w);
     for (int j = 0; ok && j < nblk; ++j) {
       const uint32_t s = kv_cnt % kTcStages;
       if (kv_cnt >= static_cast<uint32_t>(kTcStages) &&
-          !mbar_wait(&bars->kv_empty[s], ((kv_cnt / kTcStages) - 1) & 1, abort_flag, p.err,
+          !warp_wait(&bars->kv_empty[s], ((kv_cnt / kTcStages) - 1) & 1, abort_flag, p.err,
                      kErrTimeoutProducer)) {
         ok = false;
         break;
       }
       int c1, c2;
       box_coords(p.k_token_major, ks, p.heads, w.seq, w.head, j * kTcKeys, c1, c2);
-      mbar_arrive_expect_tx(&bars->k_full[s], kTileBytes);
-      tma_load_3d(sK + s * kTileBytes, tmK, &bars->k_full[s], 0, c1, c2);
+      mbar_arrive_expect_tx_w(&bars->k_full[s], kTileBytes);
+      tma_load_3d_w(sK + s * kTileBytes, tmK, &bars->k_full[s], 0, c1, c2);
       box_coords(p.v_token_major, ks, p.heads, w.seq, w.head, j * kTcKeys, c1, c2);
-      mbar_arrive_expect_tx(&bars->v_full[s], kTileBytes);
-      tma_load_3d(sV + s * kTileBytes, tmV, &bars->v_full[s], 0, c1, c2);
+      mbar_arrive_expect_tx_w(&bars->v_full[s], kTileBytes);
+      tma_load_3d_w(sV + s * kTileBytes, tmV, &bars->v_full[s], 0, c1, c2);
       ++kv_cnt;
     }
   }
@@ -190,17 +190,17 @@ __device__ __forceinline__ bool issue_s(int t, bool first_of_unit, bool last_of_
   volatile int* abort_flag = &bars->abort_flag;
   const uint32_t s = g % kTcStages;
   if (st.k_ready != g + 1) {
-    if (!mbar_wait(&bars->k_full[s], (g / kTcStages) & 1, abort_flag, err, kErrTimeoutMma))
+    if (!warp_wait(&bars->k_full[s], (g / kTcStages) & 1, abort_flag, err, kErrTimeoutMma))
       return false;
     st.k_ready = g + 1;
   }
   if (first_of_unit) {
-    if (!mbar_wait(&bars->q_full[t], st.q_use[t] & 1, abort_flag, err, kErrTimeoutMma)) return false;
+    if (!warp_wait(&bars->q_full[t], st.q_use[t] & 1, abort_flag, err, kErrTimeoutMma)) return false;
     ++st.q_use[t];
   }
   // S_t is about to be overwritten: the softmax must have read the last one.
   if (st.s_cnt[t] > 0 &&
-      !mbar_wait(&bars->sc_done[t], (st.s_cnt[t] - 1) & 1, abort_flag, err, kErrTimeoutMma))
+      !warp_wait(&bars->sc_done[t], (st.s_cnt[t] - 1) & 1, abort_flag, err, kErrTimeoutMma))
     return false;
   tc_fence_after();
   constexpr uint32_t idesc = idesc_f16(AB_F16 ? 0u : 1u, kTcRows, kTcKeys, 0, 0);
@@ -208,10 +208,10 @@ __device__ __forceinline__ bool issue_s(int t, bool first_of_unit, bool last_of_
   const uint64_t dk = smem_desc_sw128(smem_u32(sK + s * kTileBytes), 16, 1024);
 #pragma unroll
   for (int k = 0; k < 4; ++k)  // K = 64 = 4 x 16; +32 bytes per step inside the swizzle atom
-    mma_ss(tmem + kColS + t * 128, dq + 2 * k, dk + 2 * k, idesc, k > 0 ? 1u : 0u);
-  mma_commit(&bars->s_full[t]);
+    mma_ss_w(tmem + kColS + t * 128, dq + 2 * k, dk + 2 * k, idesc, k > 0 ? 1u : 0u);
+  mma_commit_w(&bars->s_full[t]);
   ++st.s_cnt[t];
-  if (last_of_unit) mma_commit(&bars->q_empty[t]);
+  if (last_of_unit) mma_commit_w(&bars->q_empty[t]);
   return true;
 }
 
@@ -265,22 +265,22 @@ __device__ __forceinline__ void run_mma(const TcParams& p, int t, uint8_t* sQ, u
                          p.err))
       return;
     const uint32_t s = g % kTcStages;
-    if (!mbar_wait(&bars->v_full[s], (g / kTcStages) & 1, abort_flag, p.err, kErrTimeoutMma)) return;
+    if (!warp_wait(&bars->v_full[s], (g / kTcStages) & 1, abort_flag, p.err, kErrTimeoutMma)) return;
     if (j < cur_tb) {
-      if (!mbar_wait(&bars->p_full[t], st.pv_cnt[t] & 1, abort_flag, p.err, kErrTimeoutMma))
+      if (!warp_wait(&bars->p_full[t], st.pv_cnt[t] & 1, abort_flag, p.err, kErrTimeoutMma))
         return;
       tc_fence_after();
       const uint64_t dv = smem_desc_sw128(smem_u32(sV + s * kTileBytes), 8192, 1024);
       const uint32_t tp = tmem + kColP + t * 64;  // P_t: bf16 pairs
 #pragma unroll
       for (int k = 0; k < 8; ++k)  // 128 keys = 8 x 16; V advances 16 rows = 2048 B per step
-        mma_ts(tmem + kColO + t * 64, tp + k * 8, dv + k * (2048 >> 4), idesc_pv,
+        mma_ts_w(tmem + kColO + t * 64, tp + k * 8, dv + k * (2048 >> 4), idesc_pv,
                (j > 0 || k > 0) ? 1u : 0u);
-      mma_commit(&bars->o_done[t]);
+      mma_commit_w(&bars->o_done[t]);
       ++st.pv_cnt[t];
-      mma_commit(&bars->kv_empty[s]);
+      mma_commit_w(&bars->kv_empty[s]);
     } else {
-      mbar_arrive(&bars->kv_empty[s]);
+      mbar_arrive_w(&bars->kv_empty[s]);
     }
     if (next_first && boundary &&
         !issue_s<AB_F16>(t, true, nxt_tb == 1, g + 1, st, sQ, sK, tmem, bars, p.err))
@@ -667,15 +667,13 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   const uint32_t tmem = bars->tmem_base;
 
   if (warp == kWarpProducer) {
-    if (lane == 0) run_producer(&tmQ, &tmK, &tmV, p, sQ, sK, sV, bars);
+    run_producer(&tmQ, &tmK, &tmV, p, sQ, sK, sV, bars);
   } else if (warp == kWarpMma0 || warp == kWarpMma0 + 1) {
-    if (lane == 0) {
-      run_mma<AB_F16>(p, warp - kWarpMma0, sQ, sK, sV, tmem, bars);
-      // Wait for every MMA either thread issued before TMEM is released.
-      int none = 0;
-      mma_commit(&bars->drain);
-      mbar_wait(&bars->drain, 0, &none, p.err, kErrTimeoutDrain);
-    }
+    run_mma<AB_F16>(p, warp - kWarpMma0, sQ, sK, sV, tmem, bars);
+    // Wait for every MMA either warp issued before TMEM is released.
+    int none = 0;
+    mma_commit_w(&bars->drain);
+    mbar_wait(&bars->drain, 0, &none, p.err, kErrTimeoutDrain);
   } else {
     run_softmax<AB_F16, CAUSAL>(p, tmem, bars, &tmO, sO);
     if (lane == 0 && p.o_tma) bulk_wait_all();  // output stores complete before exit
