@@ -320,11 +320,12 @@ __device__ __forceinline__ void store_row_quarter(const TcParams& p, const TcUni
 }
 
 // Which pairs take the polynomial exp2 (FMA pipe) instead of MUFU ex2:
-// kPolyOf8 of every 8.  MUFU sustains 16 ex2 per clock per SM; the
-// polynomial costs about ten issue slots per element, and with the softmax
-// issue-bound the measured best on the long-form encoder workload is 0 (the
-// path stays available for a kernel whose MUFU is the tighter limit).
-constexpr int kPolyOf8 = 0;
+// kPolyOf8 of every 8 (full blocks only; a block with masked keys uses MUFU
+// throughout).  MUFU sustains 16 ex2 per clock per SM and the exponentials
+// of a block pair need 2048 of its cycles; the polynomial costs about ten
+// issue slots per pair on the FMA pipe.  Measured on the long-form encoder
+// workload: 0 -> 712, 1 -> 723, 2 -> 731, 3 -> 706 TFLOP/s.
+constexpr int kPolyOf8 = 2;
 
 // f32 += one 16-bit half of a packed pair, in one instruction.
 template <int AB_F16>
