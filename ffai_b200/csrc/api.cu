@@ -357,7 +357,16 @@ int prepare_work(ffai_attn_ctx* ctx, const std::vector<int>& q_start, const std:
   // units into 2r one-tile units (at the end of the list, so the full waves
   // keep their CTAs) lets the last wave finish in about the time of one tile.
   const long long G = std::min<long long>(static_cast<long long>(units.size()), ctx->num_sms);
-  if (G > 0 && static_cast<long long>(units.size()) > G) {
+  if (2 * static_cast<long long>(units.size()) <= ctx->num_sms) {
+    // A batch too small for one wave (the single 6-head window of a small
+    // Whisper): one-tile units put twice as many SMs to work.
+    std::vector<int4> all;
+    all.swap(units);
+    for (const int4& t : all) {
+      units.push_back(make_int4(t.x, t.y, t.z, 1));
+      if (t.w == 2) units.push_back(make_int4(t.x, t.y, t.z + kTcRows, 1));
+    }
+  } else if (G > 0 && static_cast<long long>(units.size()) > G) {
     const long long r = static_cast<long long>(units.size()) % G;
     if (r > 0 && 2 * r <= G) {
       std::vector<int4> tail(units.end() - r, units.end());
