@@ -417,7 +417,8 @@ def bench_decode(steps: int, peaks, cpu_budget: float):
     legs = {}
     # Cross-attention caches are written once per utterance (kv_stable: the
     # kernel may copy them before the preceding kernel finishes); the
-    # self-attention cache gets its newest key from the preceding kernel.
+    # self-attention cache gets only its newest key from the preceding kernel
+    # (kv_append_only: the older keys may be copied early).
     cases = [("cross", workloads.C3_CROSS_KEYS, True)] + [
         ("self", n, False) for n in workloads.C3_SELF_KEYS]
     for kind, keys, stable in cases:
@@ -425,7 +426,8 @@ def bench_decode(steps: int, peaks, cpu_budget: float):
         layers = min(256, max(24, math.ceil(2 * L2_BYTES / bytes_per)))
         caches = [workloads.decode_inputs(keys, seed=100 + l, device=dev) for l in range(layers)]
         outs = [torch.empty(5, 12, 1, 64, device=dev) for _ in range(layers)]
-        calls = [lambda c=c, o=o: attention.decode(c[0], c[1], c[2], out=o, kv_stable=stable)
+        calls = [lambda c=c, o=o: attention.decode(c[0], c[1], c[2], out=o, kv_stable=stable,
+                                                   kv_append_only=not stable)
                  for c, o in zip(caches, outs)]
         t = graph_seconds(calls, max(5, min(steps, 50)))
         r = {"rows": rows, "us": round(t * 1e6, 2), "gbs": round(bytes_per / t / 1e9, 1),

@@ -156,13 +156,16 @@ def prefill(q, k, v, *, scale: float = 1.0, q_layout="heads", k_layout="heads",
 
 
 def decode(q, k, v, *, scale: float = 1.0, k_layout="heads", kv_len=None, out_dtype=torch.float32,
-           with_lse=False, num_splits=0, causal=False, q_offset=0, out=None, kv_stable=False):
+           with_lse=False, num_splits=0, causal=False, q_offset=0, out=None, kv_stable=False,
+           kv_append_only=False):
     """One decode step: q (B,H,1,64) against a K/V cache.
 
     k is (B,H,cap,64) ("heads") or (B,H,64,cap) ("kt"); v is (B,H,cap,64);
     `kv_len` <= cap keys are attended (default: all).  `kv_stable`: no work
     queued earlier on the stream writes k/v, so the kernel may start copying
-    them before the preceding kernel finishes.  Returns (B,H,1,64).
+    them before the preceding kernel finishes.  `kv_append_only`: that work
+    writes at most the newest key (kv_len - 1), so the others may be copied
+    early.  Returns (B,H,1,64).
     """
     dev = _need_cuda(q, k, v)
     B, H, qlen = _dims(q, "heads")
@@ -174,7 +177,9 @@ def decode(q, k, v, *, scale: float = 1.0, k_layout="heads", kv_len=None, out_dt
     d = _abi.new_desc(batch=B, heads=H, q_len=qlen, kv_len=Nk, kv_capacity=cap,
                       q_dtype=_DT[q.dtype], kv_dtype=_DT[k.dtype], out_dtype=_DT[out.dtype],
                       k_layout=_LAYOUT[k_layout], causal=int(causal), q_offset=q_offset,
-                      scale=scale, flags=_abi.FLAG_KV_STABLE if kv_stable else 0)
+                      scale=scale,
+                      flags=(_abi.FLAG_KV_STABLE if kv_stable else 0)
+                      | (_abi.FLAG_KV_APPEND_ONLY if kv_append_only else 0))
     ctx = context(dev.index)
     st = _abi.load().ffai_attn_decode(ctx, ctypes.byref(d), _ptr(q), _ptr(k), _ptr(v), _ptr(out),
                                       _ptr(lse), num_splits, _stream(dev))

@@ -595,6 +595,7 @@ int decode_impl(ffai_attn_ctx* ctx, const ffai_attn_desc* d, const void* q, cons
     p.scale_log2 = d->scale * 1.4426950408889634f;
     p.err = ctx->d_err;
     p.kv_stable = (d->flags & FFAI_ATTN_FLAG_KV_STABLE) != 0;
+    p.kv_append_only = !p.kv_stable && (d->flags & FFAI_ATTN_FLAG_KV_APPEND_ONLY) != 0;
     FFAI_CUDA(ctx, launch_decode_cluster(p, S, kpc, s));
     return FFAI_ATTN_OK;
   }

@@ -369,12 +369,21 @@ __global__ void __launch_bounds__(kClThreads, 2) decode_cluster_kernel(DecodePar
   const size_t base = PAGED ? 0 : (static_cast<size_t>(row) * p.cap + k0) * 64;
   if (warp == kClWarps) {
     // Producer: all of the range's stages at once, then refills as warps free them.
-    if (!p.kv_stable) griddep_wait();
+    // With kv_append_only, only the row's newest key may still be written by
+    // the preceding kernel: the stages before the one that holds it are
+    // copied first, and the wait comes before that stage.
+    const bool early = p.kv_stable || (!PAGED && p.kv_append_only);
+    if (!early) griddep_wait();
     if constexpr (PAGED) __syncwarp();  // s_page written by the warp's lanes
     if (lane == 0) {
       int issued = 0;
+      bool waited = !early || p.kv_stable;
       for (int c = 0; c < nch; ++c) {
         const int st = c % kClStages;
+        if (!waited && k0 + (c + 1) * KS >= len) {  // this stage holds key len - 1
+          griddep_wait();
+          waited = true;
+        }
         if (c >= kClStages &&
             !mbar_wait(&empty[st], ((c / kClStages) - 1) & 1, &s_abort, p.err, kErrTimeoutProducer))
           break;

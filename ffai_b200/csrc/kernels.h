@@ -40,6 +40,8 @@ struct DecodeParams {
   float scale_log2;
   unsigned* err;  // device error word (bounded waits of the cluster kernel)
   int kv_stable;  // cluster kernel: copy K/V before the programmatic-dependency wait
+  int kv_append_only;  // cluster kernel: only key kv_len - 1 may be written by the
+                       // preceding kernel; copy the others before the wait
   // paged caches (launch_decode_paged): k, v are pools of pages of kPageKeys
   // keys, (num_pages, heads, kPageKeys, 64); row = b * heads + h
   const int* block_table;  // (batch, max_pages) page ids

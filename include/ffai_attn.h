@@ -70,6 +70,13 @@ extern "C" {
  * utterance); false for a self-attention cache whose newest key the
  * preceding kernel appends.  No reference counterpart. */
 #define FFAI_ATTN_FLAG_KV_STABLE 0x2u
+/* Decode only: work queued earlier on the same stream writes at most the
+ * cache's newest key (position kv_len - 1 of every row), as the decoder's
+ * self-attention append does just before its decode.  The kernel copies the
+ * other keys before waiting for that work and the newest after, so the copy
+ * of the cache overlaps the preceding kernels.  Implied by KV_STABLE.  No
+ * reference counterpart. */
+#define FFAI_ATTN_FLAG_KV_APPEND_ONLY 0x4u
 
 /* ---- operations, for ffai_attn_check ---- */
 #define FFAI_OP_PREFILL 0

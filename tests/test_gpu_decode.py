@@ -155,3 +155,34 @@ def test_decode_kv_stable_same_bits():
     a = attention.decode(qd, kd, vd).clone()
     b = attention.decode(qd, kd, vd, kv_stable=True)
     assert torch.equal(a, b)
+
+
+@pytest.mark.parametrize("keys", [1, 64, 65, 200, 448, 1500])
+def test_decode_kv_append_only_same_bits(keys):
+    # copying the older keys before the dependency wait changes no result
+    q, k, v = workloads.decode_inputs(keys, seed=22)
+    qd, kd, vd = q.to(DEV), k.to(DEV), v.to(DEV)
+    a = attention.decode(qd, kd, vd).clone()
+    b = attention.decode(qd, kd, vd, kv_append_only=True)
+    assert torch.equal(a, b)
+
+
+def test_decode_kv_append_only_sees_the_appended_key(oracle):
+    """The self-attention step: the newest key and value are written by a
+    kernel on the same stream just before the decode that attends them; with
+    kv_append_only the decode copies the older keys early but must see them."""
+    keys, cap = 300, 448
+    q, k, v = workloads.decode_inputs(cap, seed=23)
+    kd, vd = k.to(DEV).clone(), v.to(DEV).clone()
+    qd = q.to(DEV)
+    outs, refs = [], []
+    for step in range(4):
+        n = keys + step
+        kd[:, :, n - 1].mul_(-2.0)  # a kernel writing key n - 1 only
+        vd[:, :, n - 1].add_(1.0)
+        outs.append(attention.decode(qd, kd, vd, kv_len=n, kv_append_only=True))
+        refs.append((kd[:, :, :n].cpu(), vd[:, :, :n].cpu()))
+    torch.cuda.synchronize()
+    for step, (o, (kr, vr)) in enumerate(zip(outs, refs)):
+        ref = _oracle_decode(oracle, q, kr, vr)
+        assert_f32_close(f32np(o), ref, f"append step {step}")
