@@ -38,6 +38,7 @@ pub const FFAI_LAYOUT_KT: i32 = 2;
 pub const FFAI_ATTN_FLAG_CHECKED_F32: u32 = 0x1;
 pub const FFAI_ATTN_FLAG_KV_STABLE: u32 = 0x2;
 pub const FFAI_ATTN_FLAG_KV_APPEND_ONLY: u32 = 0x4;
+pub const FFAI_ATTN_FLAG_INPUTS_STABLE: u32 = 0x8;
 
 pub const FFAI_OP_PREFILL: c_int = 0;
 pub const FFAI_OP_DECODE: c_int = 1;

@@ -29,6 +29,7 @@ LAYOUT_HEADS_SPLIT, LAYOUT_TOKEN_MAJOR, LAYOUT_KT = 0, 1, 2
 FLAG_CHECKED_F32 = 0x1
 FLAG_KV_STABLE = 0x2
 FLAG_KV_APPEND_ONLY = 0x4
+FLAG_INPUTS_STABLE = 0x8
 # ops
 OP_PREFILL, OP_DECODE, OP_VARLEN = 0, 1, 2
 

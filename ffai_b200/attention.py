@@ -124,11 +124,15 @@ def _operands(tensors, layouts):
 
 def prefill(q, k, v, *, scale: float = 1.0, q_layout="heads", k_layout="heads",
             v_layout="heads", out_layout="heads", out_dtype=torch.float32, kv_len=None,
-            with_lse=False, checked=False, causal=False, q_offset=0, out=None):
+            with_lse=False, checked=False, causal=False, q_offset=0, out=None,
+            inputs_stable=False):
     """softmax(scale q k^T) v over a batch of equal-length sequences.
 
     Layouts: "heads" (B,H,N,64), "token" (B,N,H,64) and, for k only, "kt"
     (B,H,64,N).  Returns out (and lse (B,H,Nq) or (H,B*Nq) when with_lse).
+    `inputs_stable`: no work still pending on the stream writes q/k/v, so the
+    kernel may read them while the preceding kernel finishes (back-to-back
+    launches over independent batches overlap).
     """
     dev = _need_cuda(q, k, v, strided=True)
     B, H, Nq = _dims(q, q_layout)
@@ -147,7 +151,8 @@ def prefill(q, k, v, *, scale: float = 1.0, q_layout="heads", k_layout="heads",
                       q_layout=_LAYOUT[q_layout], k_layout=_LAYOUT[k_layout],
                       v_layout=_LAYOUT[v_layout], out_layout=_LAYOUT[out_layout],
                       causal=int(causal), q_offset=q_offset, scale=scale,
-                      flags=_abi.FLAG_CHECKED_F32 if checked else 0, token_stride=ts)
+                      flags=(_abi.FLAG_CHECKED_F32 if checked else 0)
+                      | (_abi.FLAG_INPUTS_STABLE if inputs_stable else 0), token_stride=ts)
     ctx = context(dev.index)
     st = _abi.load().ffai_attn_prefill(ctx, ctypes.byref(d), _ptr(q), _ptr(k), _ptr(v), _ptr(out),
                                        _ptr(lse), _stream(dev))
@@ -212,10 +217,11 @@ def decode_static(q, k, v, *, scale: float = 1.0, k_layout="heads", kv_len=None,
 
 
 def varlen(q, k, v, cu_seqlens_q, cu_seqlens_k=None, *, scale: float = 1.0,
-           out_dtype=torch.float32, with_lse=False, out=None):
+           out_dtype=torch.float32, with_lse=False, out=None, inputs_stable=False):
     """Ragged prefill over packed segments: q/k/v (T,H,64), host cu_seqlens.
 
     Segment s attends only within itself.  Returns out (T,H,64) [, lse (H,T)].
+    `inputs_stable` as for prefill().
     """
     dev = _need_cuda(q, k, v, strided=True)
     if q.dim() != 3 or q.shape[-1] != 64:
@@ -233,7 +239,8 @@ def varlen(q, k, v, cu_seqlens_q, cu_seqlens_k=None, *, scale: float = 1.0,
     d = _abi.new_desc(heads=H, q_dtype=_DT[q.dtype], kv_dtype=_DT[k.dtype],
                       out_dtype=_DT[out.dtype], q_layout=_abi.LAYOUT_TOKEN_MAJOR,
                       k_layout=_abi.LAYOUT_TOKEN_MAJOR, v_layout=_abi.LAYOUT_TOKEN_MAJOR,
-                      out_layout=_abi.LAYOUT_TOKEN_MAJOR, scale=scale, token_stride=ts)
+                      out_layout=_abi.LAYOUT_TOKEN_MAJOR, scale=scale, token_stride=ts,
+                      flags=_abi.FLAG_INPUTS_STABLE if inputs_stable else 0)
     ctx = context(dev.index)
     st = _abi.load().ffai_attn_varlen(ctx, ctypes.byref(d), arr_q, arr_k, n_seg, _ptr(q), _ptr(k),
                                       _ptr(v), _ptr(out), _ptr(lse), _stream(dev))

@@ -309,16 +309,19 @@ int make_map(ffai_attn_ctx* ctx, CUtensorMap* map, const void* base, bool token_
 
 // Build (or reuse) the device work list: per-sequence offsets/lengths and
 // units of up to 256 query rows, longest sequences first.
+// keep_tail: leave a short last wave of two-tile units as it is (the caller
+// launches back to back with stable inputs, so the next launch fills it).
 int prepare_work(ffai_attn_ctx* ctx, const std::vector<int>& q_start, const std::vector<int>& q_len,
                  const std::vector<int>& k_start, const std::vector<int>& k_len, int H,
-                 cudaStream_t s, int causal = 0, int q_offset = 0) {
+                 cudaStream_t s, int causal = 0, int q_offset = 0, bool keep_tail = false) {
   const int nseq = static_cast<int>(q_len.size());
   std::vector<long long> key;
-  key.reserve(4 * nseq + 4);
+  key.reserve(4 * nseq + 5);
   key.push_back(H);
   key.push_back(nseq);
   key.push_back(causal);
   key.push_back(causal ? q_offset : 0);
+  key.push_back(keep_tail);
   for (int i = 0; i < nseq; ++i) {
     key.push_back(q_start[i]);
     key.push_back(q_len[i]);
@@ -366,7 +369,7 @@ int prepare_work(ffai_attn_ctx* ctx, const std::vector<int>& q_start, const std:
       units.push_back(make_int4(t.x, t.y, t.z, 1));
       if (t.w == 2) units.push_back(make_int4(t.x, t.y, t.z + kTcRows, 1));
     }
-  } else if (G > 0 && static_cast<long long>(units.size()) > G) {
+  } else if (!keep_tail && G > 0 && static_cast<long long>(units.size()) > G) {
     const long long r = static_cast<long long>(units.size()) % G;
     if (r > 0 && 2 * r <= G) {
       std::vector<int4> tail(units.end() - r, units.end());
@@ -415,7 +418,8 @@ struct Operand {
 
 int run_tc(ffai_attn_ctx* ctx, const Operand& q, const Operand& k, const Operand& v, int H,
            int ab_f16, void* o, int out_bf16, bool out_tm, long long out_rows, float* lse,
-           long long lse_tokens, float scale, cudaStream_t s, int causal = 0, int q_offset = 0) {
+           long long lse_tokens, float scale, cudaStream_t s, int causal = 0, int q_offset = 0,
+           bool inputs_stable = false) {
   if (reinterpret_cast<uintptr_t>(o) % 8 != 0)
     return set_error(ctx, FFAI_ATTN_ERR_INVALID, "prefill output must be 8-byte aligned");
   CUtensorMap tq, tk, tv;
@@ -455,6 +459,7 @@ int run_tc(ffai_attn_ctx* ctx, const Operand& q, const Operand& k, const Operand
   p.causal = causal;
   p.q_offset = q_offset;
   p.o_tma = o_tma ? 1 : 0;
+  p.inputs_stable = inputs_stable ? 1 : 0;
   const int grid = std::min(ctx->wl_units, ctx->num_sms);
   if (grid <= 0) return FFAI_ATTN_OK;
   FFAI_CUDA(ctx, launch_prefill_tc(tq, tk, tv, to, p, grid, ab_f16, s));
@@ -551,7 +556,9 @@ int prefill_impl(ffai_attn_ctx* ctx, const ffai_attn_desc* d, const void* q, con
     qs[b] = b * Nq;
     ks[b] = b * cap;  // token-major K/V are never staged, so they keep `cap`
   }
-  int st = prepare_work(ctx, qs, ql, ks, kl, H, s, d->causal, d->q_offset);
+  // Staged operands are written by the staging kernels just before.
+  const bool stable = (d->flags & FFAI_ATTN_FLAG_INPUTS_STABLE) && !stage;
+  int st = prepare_work(ctx, qs, ql, ks, kl, H, s, d->causal, d->q_offset, stable);
   if (st) return st;
   const long long BH = static_cast<long long>(B) * H;
   Operand oq{qq, q_tm, q_tm ? static_cast<long long>(B) * Nq : Nq, BH, d->token_stride};
@@ -559,7 +566,7 @@ int prefill_impl(ffai_attn_ctx* ctx, const ffai_attn_desc* d, const void* q, con
   Operand ov{vv, v_tm, v_tm ? static_cast<long long>(B) * vcap : vcap, BH, d->token_stride};
   return run_tc(ctx, oq, ok, ov, H, ab_f16, o, d->out_dtype == FFAI_DT_BF16,
                 d->out_layout == FFAI_LAYOUT_TOKEN_MAJOR, Nq, lse, static_cast<long long>(B) * Nq,
-                d->scale, s, d->causal, d->q_offset);
+                d->scale, s, d->causal, d->q_offset, stable);
 }
 
 int decode_impl(ffai_attn_ctx* ctx, const ffai_attn_desc* d, const void* q, const void* k,
@@ -841,13 +848,14 @@ int ffai_attn_varlen(ffai_attn_ctx* ctx, const ffai_attn_desc* d, const int32_t*
   DeviceGuard g(ctx->device);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   ProfScope ps(ctx, FFAI_OP_VARLEN, s, "ffai_attn_varlen");
-  st = prepare_work(ctx, qs, ql, ks, kl, d->heads, s);
+  const bool stable = (d->flags & FFAI_ATTN_FLAG_INPUTS_STABLE) != 0;
+  st = prepare_work(ctx, qs, ql, ks, kl, d->heads, s, 0, 0, stable);
   if (st) return st;
   if (Tq == 0) return FFAI_ATTN_OK;
   const Operand oq{q, true, Tq, 1, d->token_stride}, ok{k, true, Tk, 1, d->token_stride},
       ov{v, true, Tk, 1, d->token_stride};
   return run_tc(ctx, oq, ok, ov, d->heads, d->q_dtype == FFAI_DT_F16, o,
-                d->out_dtype == FFAI_DT_BF16, true, 0, lse, Tq, d->scale, s);
+                d->out_dtype == FFAI_DT_BF16, true, 0, lse, Tq, d->scale, s, 0, 0, stable);
 }
 
 int ffai_attn_prefill_host(ffai_attn_ctx* ctx, const ffai_attn_desc* d, const void* q,

@@ -267,6 +267,8 @@ struct TcParams {
   int causal;    // key j visible to query row i (within its sequence) iff j <= q_offset + i
   int q_offset;  // >= 0
   int o_tma;     // 1: bf16 output through the tmO tensor map (16-row boxes)
+  int inputs_stable;  // 1: q/k/v not written by the preceding kernel; read them
+                      // before the programmatic-dependency wait
 };
 
 // Key blocks (of kTcKeys) that tile t (0, 1) of a unit needs: all of the

@@ -13,7 +13,7 @@
 //
 //   warp 16     TMA producer: Q tiles, then a 3-stage ring of K/V blocks of
 //               128 keys (16 KB each, 128-byte swizzle).  Also owns TMEM.
-//   warps 17,18 MMA issuers, one thread per tile: S_t = Q_t K^T   (M=128, N=128, K=64)
+//   warps 17,18 MMA issuers, one warp per tile:   S_t = Q_t K^T   (M=128, N=128, K=64)
 //                                         O_t += P_t V    (M=128, N=64,  K=128)
 //               with P_t read straight from tensor memory (the "A in TMEM"
 //               form), so probabilities never touch shared memory.  S_t(j+1)
@@ -39,6 +39,13 @@
 //
 // Every wait is bounded (common.cuh); on a timeout the CTA raises an error
 // bit, drains its MMAs and TMA loads, frees TMEM and exits.
+//
+// The kernel is a programmatic dependent of the preceding kernel on its
+// stream and lets its own dependents launch once all its CTAs are resident.
+// It waits for the preceding kernel before the producer's first load (unless
+// the caller marks q/k/v stable) and before the first store of its output,
+// so with stable inputs back-to-back launches over independent batches run
+// the next batch's units on the SMs the previous launch's last wave frees.
 #include <atomic>
 
 #include "common.cuh"
@@ -136,6 +143,9 @@ __device__ __forceinline__ void run_producer(const CUtensorMap* tmQ, const CUten
   uint32_t q_use[2] = {0, 0};
   uint32_t kv_cnt = 0;
   bool ok = true;
+  // The operands may come from the preceding kernel (programmatic dependent
+  // launch) unless the caller says they do not.
+  if (!p.inputs_stable) griddep_wait();
   for (int u = blockIdx.x; ok && u < p.num_units; u += gridDim.x) {
     TcUnit w;
     unit_at(p, u, w);
@@ -438,6 +448,7 @@ __device__ __forceinline__ void run_softmax(const TcParams& p, uint32_t tmem, Tc
   const float sl2 = p.scale_log2;
   uint32_t s_cnt = 0, pv_cnt = 0;
 
+  bool dependency_done = false;
   for (int u = blockIdx.x; u < p.num_units; u += gridDim.x) {
     TcUnit w;
     unit_at(p, u, w);
@@ -552,6 +563,11 @@ __device__ __forceinline__ void run_softmax(const TcParams& p, uint32_t tmem, Tc
     // Epilogue: O_t / l to global memory.
     if (!warp_wait(&bars->o_done[t], (pv_cnt - 1) & 1, abort_flag, p.err, kErrTimeoutSoftmax)) return;
     tc_fence_after();
+    // out and lse may still be read or written by the preceding kernel.
+    if (!dependency_done) {
+      griddep_wait();
+      dependency_done = true;
+    }
     uint32_t orr[32];
     tmem_ld_16x256b_x8(tO, orr);
     tmem_wait_ld();
@@ -666,6 +682,10 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = bars->tmem_base;
+  // Every CTA is resident: the next kernel on the stream may start its CTAs
+  // on the SMs this grid leaves (it waits for this grid before it reads what
+  // this grid writes).
+  griddep_launch_dependents();
 
   if (warp == kWarpProducer) {
     run_producer(&tmQ, &tmK, &tmV, p, sQ, sK, sV, bars);
@@ -714,8 +734,19 @@ cudaError_t launch_prefill_tc(const CUtensorMap& tmQ, const CUtensorMap& tmK,
     if (e != cudaSuccess) return e;
     configured[which][dev].store(true, std::memory_order_release);
   }
-  kern<<<grid, kTcThreads, kSmemBytes, s>>>(tmQ, tmK, tmV, tmO, p);
-  return cudaGetLastError();
+  // A programmatic dependent of the preceding kernel: see run_producer and
+  // the epilogue for the two waits.
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(kTcThreads);
+  cfg.dynamicSmemBytes = kSmemBytes;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kern, tmQ, tmK, tmV, tmO, p);
 }
 
 }  // namespace ffai

@@ -77,6 +77,19 @@ extern "C" {
  * of the cache overlaps the preceding kernels.  Implied by KV_STABLE.  No
  * reference counterpart. */
 #define FFAI_ATTN_FLAG_KV_APPEND_ONLY 0x4u
+/* Prefill and varlen (tensor-core path): no work still pending on the stream
+ * when the call is made writes q, k or v (they were written before a
+ * synchronisation, or are earlier launches' untouched inputs).  The prefill
+ * kernel is always launched as a programmatic dependent: it waits for the
+ * preceding kernel before its first read of q/k/v and again before its first
+ * write of out/lse.  With this flag it reads and computes before the first
+ * of those waits, so a launch over one batch fills the SMs that the preceding
+ * launch's last wave leaves idle; the work list then keeps two-tile units in
+ * a short last wave (the next launch fills the tail) instead of splitting
+ * them.  Ignored where the library stages the operands itself (f32 operands,
+ * the K^T layout): the staging kernel writes what the prefill kernel reads.
+ * No reference counterpart. */
+#define FFAI_ATTN_FLAG_INPUTS_STABLE 0x8u
 
 /* ---- operations, for ffai_attn_check ---- */
 #define FFAI_OP_PREFILL 0

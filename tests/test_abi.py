@@ -154,3 +154,13 @@ def test_flash_check_applies_the_reference_decline_rules(lib):
     assert check(t4((1, 6, 1500, 64), dev=-1), *enc[1:]) == _abi.DECLINED
     assert check(enc[0], t4((1, 6, 64, 1500), dev=1), enc[2]) == _abi.DECLINED
     assert "device" in _abi.last_error(None)
+
+
+def test_python_flag_constants_match_the_header():
+    text = open(HEADER).read()
+    defines = {n: int(v, 0) for n, v in
+               re.findall(r"#define FFAI_ATTN_(FLAG_\w+) (0x[0-9a-fA-F]+)u", text)}
+    assert set(defines) == {"FLAG_CHECKED_F32", "FLAG_KV_STABLE", "FLAG_KV_APPEND_ONLY",
+                            "FLAG_INPUTS_STABLE"}
+    for name, value in defines.items():
+        assert getattr(_abi, name) == value, name

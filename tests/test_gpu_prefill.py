@@ -327,3 +327,78 @@ def test_bf16_output_varlen_equals_rounded_f32():
     f32 = attention.varlen(q, k, v, cu, scale=S, out_dtype=torch.float32)
     b16 = attention.varlen(q, k, v, cu, scale=S, out_dtype=torch.bfloat16)
     assert torch.equal(b16, f32.to(torch.bfloat16))
+
+
+def test_inputs_stable_back_to_back_equals_single_launches():
+    """Launches over independent batches with FFAI_ATTN_FLAG_INPUTS_STABLE run
+    back to back (each reads its operands while the previous one finishes,
+    and the work list keeps a short last wave of two-tile units): every
+    result equals the same batch launched alone without the flag, bitwise.
+    4 x 20 x 1500 is 480 units, a last wave of 36 on 148 SMs."""
+    batches = [tuple(t.to(DEV) for t in _inputs(4, 20, 1500, seed=90 + i)) for i in range(4)]
+    want = [attention.prefill(*b, scale=S, out_dtype=torch.bfloat16) for b in batches]
+    torch.cuda.synchronize()
+    for rounds in range(2):
+        got = [attention.prefill(*b, scale=S, out_dtype=torch.bfloat16, inputs_stable=True)
+               for b in batches]
+        torch.cuda.synchronize()
+        for i, (g, w) in enumerate(zip(got, want)):
+            assert torch.equal(g, w), f"batch {i}, round {rounds}"
+    attention.sync(0)
+
+
+def test_inputs_stable_launch_writes_what_the_previous_launch_reads():
+    """Write after read across launches: launch B (stable inputs) writes its
+    output into the buffer launch A reads as q.  B may start while A runs, so
+    its first store waits for A; A must see the old q."""
+    qa, ka, va = (t.to(DEV) for t in _inputs(6, 20, 1500, seed=95))
+    qb, kb, vb = (t.to(DEV) for t in _inputs(6, 20, 1500, seed=96))
+    want_a = attention.prefill(qa, ka, va, scale=S, out_dtype=torch.bfloat16)
+    want_b = attention.prefill(qb, kb, vb, scale=S, out_dtype=torch.bfloat16)
+    qa_keep = qa.clone()
+    torch.cuda.synchronize()
+    got_a = attention.prefill(qa, ka, va, scale=S, out_dtype=torch.bfloat16, inputs_stable=True)
+    attention.prefill(qb, kb, vb, scale=S, out=qa, inputs_stable=True)  # overwrites A's q
+    torch.cuda.synchronize()
+    assert torch.equal(got_a, want_a)
+    assert torch.equal(qa, want_b)
+    assert not torch.equal(qa, qa_keep)
+    attention.sync(0)
+
+
+@pytest.mark.parametrize("stable", [False, True])
+def test_prefill_reads_the_preceding_prefill_output(stable):
+    """Read after write: launch B's q is launch A's output, with no flag on B
+    (B waits for A before its first load).  With the flag on A only, A still
+    waits for the kernel before it before storing."""
+    q, k, v = (t.to(DEV) for t in _inputs(6, 20, 1500, seed=97))
+    torch.cuda.synchronize()  # the flag on A: nothing pending writes A's inputs
+    a = attention.prefill(q, k, v, scale=S, out_dtype=torch.bfloat16, inputs_stable=stable)
+    b = attention.prefill(a, k, v, scale=S, out_dtype=torch.bfloat16)
+    torch.cuda.synchronize()
+    a_ref = attention.prefill(q, k, v, scale=S, out_dtype=torch.bfloat16)
+    torch.cuda.synchronize()
+    b_ref = attention.prefill(a_ref.clone(), k, v, scale=S, out_dtype=torch.bfloat16)
+    torch.cuda.synchronize()
+    assert torch.equal(a, a_ref) and torch.equal(b, b_ref)
+    attention.sync(0)
+
+
+def test_inputs_stable_varlen_and_staged_operands():
+    """varlen with the flag equals varlen without; f32 operands (staged by the
+    library, so the flag does not apply to the kernel) likewise."""
+    lengths = workloads.ragged_lengths()[:64]
+    q, k, v, cu = workloads.ragged_inputs(lengths, device=DEV)
+    want = attention.varlen(q, k, v, cu, scale=S, out_dtype=torch.bfloat16)
+    torch.cuda.synchronize()
+    got = [attention.varlen(q, k, v, cu, scale=S, out_dtype=torch.bfloat16, inputs_stable=True)
+           for _ in range(3)]
+    torch.cuda.synchronize()
+    for g in got:
+        assert torch.equal(g, want)
+    qf, kf, vf = (t.float().to(DEV) for t in _inputs(2, 6, 700, seed=98))
+    want = attention.prefill(qf, kf, vf, scale=S)
+    got = attention.prefill(qf, kf, vf, scale=S, inputs_stable=True)
+    torch.cuda.synchronize()
+    assert torch.equal(got, want)
+    attention.sync(0)
