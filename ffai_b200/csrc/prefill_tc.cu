@@ -365,26 +365,26 @@ __device__ __forceinline__ float add_half_hi(float acc, uint32_t pk) {
 // store writes: pk[2k + v] holds the keys 8k + 2 t0 and 8k + 2 t0 + 1 of row
 // v, i.e. P word 4k + t0.  Adds the rounded (packed) values to sum[v].
 //
-// m_v is integer-valued (the running max is kept as a ceiling), which lets the
-// polynomial path fold its range reduction into the score scaling:
-//   t = fma(s, sl2, 1.5*2^23 - m) = 1.5*2^23 + round(x)     (x = s*sl2 - m)
-//   f = fma(s, sl2, -(round(x) + m)) = x - round(x)           in [-0.5, 0.5]
-// both exact up to the single rounding of each FMA; 2^f by a degree-3
-// polynomial (this project's own minimax fit of 2^f on [-0.5, 0.5], max
-// relative error 7.5e-5) and round(x) spliced into the exponent field.
-// Clamping t at round(x) >= -125 keeps the splice in range; below that 2^x
-// < 2^-125 and the result is negligible whatever f is.
+// The polynomial path (FMA pipe) takes x = s * sl2 - m clamped at -125 and
+// splits it by the 1.5 * 2^23 trick: t = x + 1.5*2^23 holds round(x) in its
+// low mantissa bits (exact), f = x - round(x) in [-0.5, 0.5] (exact); 2^f by
+// a degree-3 polynomial (this project's own minimax fit of 2^f on
+// [-0.5, 0.5], max relative error 7.5e-5) and round(x) spliced into the
+// exponent field.  The clamp keeps the splice in range and f bounded: a score
+// more than 125 below the row's reference gives 2^-125 or so, negligible
+// beside the reference's 1 (an unclamped f there made the cubic, and with it
+// the spliced value, large).
 template <int AB_F16, bool kTail>
 __device__ __forceinline__ void exp_pack_rows(const float* sf, float sl2, const float (&m)[2],
                                               uint32_t (&pk)[32], float (&sum)[2]) {
   const float kMagic = 12582912.0f;  // 1.5 * 2^23
   const uint64_t c2 = f2_pack(sl2, sl2);
-  uint64_t n2[2], cm2[2];
+  const uint64_t magic2 = f2_pack(kMagic, kMagic);
+  uint64_t n2[2];
 #pragma unroll
   for (int v = 0; v < 2; ++v) {
     const float neg = (m[v] == -INFINITY) ? 0.f : -m[v];
     n2[v] = f2_pack(neg, neg);
-    cm2[v] = f2_pack(kMagic + neg, kMagic + neg);
   }
   const uint64_t kC3 = f2_pack(0.055171434f, 0.055171434f);
   const uint64_t kC2 = f2_pack(0.24261081f, 0.24261081f);
@@ -398,12 +398,13 @@ __device__ __forceinline__ void exp_pack_rows(const float* sf, float sl2, const 
       float p0, p1;
       const uint64_t sv = f2_pack(sf[4 * k + 2 * v], sf[4 * k + 2 * v + 1]);
       if (!kTail && (k % 8) < kPolyOf8) {
+        float x0, x1;
+        f2_unpack(f2_fma(sv, c2, n2[v]), x0, x1);
+        const uint64_t x = f2_pack(fmaxf(x0, -125.f), fmaxf(x1, -125.f));
+        const uint64_t t = f2_add(x, magic2);               // 1.5*2^23 + round(x)
+        const uint64_t f = f2_sub(x, f2_sub(t, magic2));    // x - round(x)
         float t0, t1;
-        f2_unpack(f2_fma(sv, c2, cm2[v]), t0, t1);
-        t0 = fmaxf(t0, kMagic - 125.f);
-        t1 = fmaxf(t1, kMagic - 125.f);
-        const uint64_t t = f2_pack(t0, t1);
-        const uint64_t f = f2_fma(sv, c2, f2_sub(cm2[v], t));  // x - round(x)
+        f2_unpack(t, t0, t1);
         uint64_t q = f2_fma(kC3, f, kC2);
         q = f2_fma(q, f, kC1);
         q = f2_fma(q, f, kC0);

@@ -402,3 +402,105 @@ def test_inputs_stable_varlen_and_staged_operands():
     torch.cuda.synchronize()
     assert torch.equal(got, want)
     attention.sync(0)
+
+
+# ------------------------------------------------ scores that grow after a unit's first block
+# Inputs that plant, in later key blocks, keys aligned with chosen queries, so
+# a row's maximum jumps by ~`alpha * 2.9` log2 units (|q|^2 ~ 16, scale 1/8)
+# while every other row sees a random jump of std ~`alpha * 0.36`.  Each jump
+# past 8 moves the row's reference and rescales O in tensor memory; at alpha
+# 60 the ordinary keys then sit ~170 log2 units below the reference, where the
+# polynomial exp2 (FMA-pipe share of a full block) must clamp its argument
+# and still give ~0.
+
+
+def _growth_inputs(B, H, N, alpha, dtype=torch.bfloat16, seed=0, first_key=300, count=40):
+    q, k, v = _inputs(B, H, N, dtype=torch.float32, seed=seed)
+    rows = torch.arange(0, min(N, 4 * count), 4)[:count]
+    keys = first_key + torch.arange(len(rows)) * 7 % max(1, N - first_key)
+    k[:, :, keys] = alpha * q[:, :, rows]
+    return q.to(dtype), k.to(dtype), v.to(dtype)
+
+
+@pytest.mark.parametrize("alpha", [10.0, 60.0])
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+def test_tc_growth_after_first_block(oracle, alpha, dtype):
+    q, k, v = _growth_inputs(2, 3, 700, alpha, dtype=dtype, seed=int(alpha))
+    ref = oracle_encoder(oracle, q, k, v, S)
+    out, lse = attention.prefill(q.to(DEV), k.to(DEV), v.to(DEV), scale=S, with_lse=True)
+    assert_bf16_close(f32np(out), ref, f"growth alpha={alpha}")
+    # The planted rows are dominated by one key, whose 16-bit P carries a
+    # rounding of up to 2^-8 relative: their LSE may differ from the exact one
+    # by up to ln(1 + 2^-8) < 4e-3 (as for a causal row with one visible key).
+    err = rowsum_error(f32np(q).reshape(6, 700, 64), f32np(k).reshape(6, 700, 64), S,
+                       f32np(lse).reshape(6, 700))
+    assert err <= 4e-3, f"LSE off by {err:.2e}"
+
+
+@pytest.mark.parametrize("alpha", [10.0, 60.0])
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+def test_tc_growth_rowsums(alpha, dtype):
+    """After large jumps of the reference the applied weights of every row
+    still sum to 1 (V = ones): the rescales of O in tensor memory and of the
+    row sum stay consistent, where a lost or doubled correction would be off
+    by orders of magnitude.  The bar is 5e-5, not the 1e-6 of ordinary rows:
+    after a jump the remaining keys weigh 2^-20 or less of the running O,
+    and the tensor core adds such products to its accumulator with less than
+    f32 precision while the f32 row sum keeps more of them (measured up to
+    1.7e-5 on these inputs)."""
+    q, k, _ = _growth_inputs(2, 4, 1500, alpha, dtype=dtype, seed=3 + int(alpha), first_key=600)
+    ones = torch.ones(2, 4, 1500, 64, dtype=dtype)
+    out = attention.prefill(q.to(DEV), k.to(DEV), ones.to(DEV), scale=S)
+    err = (out.double() - 1.0).abs().max().item()
+    assert err <= 5e-5, f"row sums off by {err:.2e}"
+
+
+@pytest.mark.parametrize("layout", ["all_token", "kt", "fused"])
+def test_tc_growth_layouts(oracle, layout):
+    """Large jumps under each operand layout."""
+    B, H, N = 2, 4, 520
+    q, k, v = _growth_inputs(B, H, N, 60.0, seed=77, first_key=260)
+    ref = oracle_encoder(oracle, q, k, v, S)
+    qd, kd, vd = q.to(DEV), k.to(DEV), v.to(DEV)
+    kw = dict(scale=S)
+    if layout == "all_token":
+        qd, kd, vd = (t.transpose(1, 2).contiguous() for t in (qd, kd, vd))
+        kw.update(q_layout="token", k_layout="token", v_layout="token")
+    elif layout == "kt":
+        kd = kd.transpose(-1, -2).contiguous()
+        kw.update(k_layout="kt")
+    else:  # views of one fused projection output (B, N, 3, H, 64)
+        qkv = torch.stack([t.transpose(1, 2) for t in (qd, kd, vd)], dim=2).contiguous()
+        qd, kd, vd = qkv[:, :, 0], qkv[:, :, 1], qkv[:, :, 2]
+        kw.update(q_layout="token", k_layout="token", v_layout="token")
+    out = attention.prefill(qd, kd, vd, **kw)
+    assert_bf16_close(f32np(out), ref, layout)
+
+
+def test_tc_growth_causal(oracle):
+    B, H, Nq, off, cap = 1, 3, 300, 148, 448
+    q, k, v = _growth_inputs(B, H, cap, 60.0, seed=78, first_key=200)
+    q = q[:, :, :Nq].contiguous()
+    kv = off + Nq
+    out = attention.prefill(q.to(DEV), k.to(DEV), v.to(DEV), scale=S, causal=True, q_offset=off,
+                            kv_len=kv)
+    ref, _ = oracle.naive_attention_f64(f32np(q), f32np(k)[:, :, :kv], f32np(v)[:, :, :kv],
+                                        scale=S, causal=True, q_offset=off)
+    assert_bf16_close(f32np(out), ref, "causal growth")
+
+
+def test_tc_growth_varlen(oracle):
+    lengths = [700, 129, 1000, 300]
+    q, k, v, cu = workloads.ragged_inputs(lengths, heads=4, seed=79)
+    q, k, v = q.float(), k.float(), v.float()
+    for s, (a, b) in enumerate(zip(cu[:-1], cu[1:])):
+        n = b - a
+        if n > 300:  # keys past the first block aligned with early queries of the same segment
+            rows = torch.arange(a, a + 120, 4)
+            keys = a + 260 + (torch.arange(len(rows)) * 11) % (n - 260)
+            k[keys] = 60.0 * q[rows]
+    q, k, v = (t.to(torch.bfloat16) for t in (q, k, v))
+    out = attention.varlen(q.to(DEV), k.to(DEV), v.to(DEV), cu, scale=S)
+    refs = _oracle_ragged(oracle, q, k, v, cu, range(len(lengths)))
+    for s, ref in refs.items():
+        assert_bf16_close(f32np(out[cu[s]:cu[s + 1]]), ref, f"segment {s}")
