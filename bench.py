@@ -614,7 +614,9 @@ def bench_projections(steps: int, dev):
     (`ffai_b200.gemm.linear`), on one c4 segment batch's tokens (16 segments x
     1500 frames, large-v3): q/k/v (N 3840), out-projection + residual, fc1 +
     FastGelu, fc2 + residual; TFLOP/s against the measured bf16 peak, beside
-    torch's cuBLAS linear on the same operands (no fused epilogue)."""
+    torch's cuBLAS linear on the same operands (no fused epilogue) and beside
+    the unfused alternative: that linear followed by torch's separate tanh
+    GELU, or by the residual add into the f32 stream (the same output)."""
     import torch
 
     from ffai_b200.gemm import linear
@@ -646,11 +648,22 @@ def bench_projections(steps: int, dev):
         out_dtype = torch.float32 if r is not None else torch.bfloat16
         out = torch.empty(T, n, device=dev, dtype=out_dtype)
         t = time_it(lambda: linear(a, w, bias, act, r, out_dtype=out_dtype, out=out), max(3, steps))
-        tb = time_it(lambda: torch.nn.functional.linear(a, w, bias.to(torch.bfloat16)), max(3, steps))
+        bias16 = bias.to(torch.bfloat16)
+        tb = time_it(lambda: torch.nn.functional.linear(a, w, bias16), max(3, steps))
+
+        def unfused():
+            y = torch.nn.functional.linear(a, w, bias16)
+            if act is not None:
+                return torch.nn.functional.gelu(y, approximate="tanh")
+            if r is not None:
+                return torch.add(r, y, out=out)
+            return y
+        tu = time_it(unfused, max(3, steps))
         flop = 2.0 * T * n * k
         res[name] = {"kernel": "gemm_tc_kernel", "m_n_k": [T, n, k], "us": round(t * 1e6, 1),
                      "tflops": round(flop / t / 1e12, 1),
-                     "torch_linear_tflops": round(flop / tb / 1e12, 1)}
+                     "torch_linear_tflops": round(flop / tb / 1e12, 1),
+                     "torch_unfused_tflops": round(flop / tu / 1e12, 1)}
     return res
 
 
@@ -860,8 +873,10 @@ def run_ours(args, dist):
     if single and not args.no_gemm:
         proj = bench_projections(max(5, min(args.steps, 20)), cur)
         fleg.append(("f_gemm", {k_: [v_["tflops"], round(v_["tflops"] / peaks["bf16_tflops"], 3),
-                                     v_["torch_linear_tflops"]] for k_, v_ in proj.items()}
-                     | {"cols": "tflops, frac, torch linear tflops", "m": 24000}))
+                                     v_["torch_linear_tflops"], v_["torch_unfused_tflops"]]
+                                for k_, v_ in proj.items()}
+                     | {"cols": "tflops, frac, torch linear tflops, torch linear + separate "
+                                "epilogue tflops", "m": 24000}))
     if single and not args.no_f16:
         f16 = bench_f16_gemv(max(5, min(args.steps, 50)), cur)
         cpu16 = f16.pop("cpu_fc1_5120x1280_b1")
