@@ -419,6 +419,28 @@ __device__ __forceinline__ void tmem_st_16x128b_x16(uint32_t taddr, const uint32
                : "memory");
 }
 
+// Two 8-column chunks of the 16x256b shape (16 columns, 8 registers).
+__device__ __forceinline__ void tmem_ld_16x256b_x2(uint32_t taddr, uint32_t (&r)[8]) {
+  asm volatile("tcgen05.ld.sync.aligned.16x256b.x2.b32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+                 "=r"(r[7])
+               : "r"(taddr));
+}
+__device__ __forceinline__ void tmem_st_16x256b_x2(uint32_t taddr, const uint32_t (&r)[8]) {
+  asm volatile("tcgen05.st.sync.aligned.16x256b.x2.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8};"
+               ::"r"(taddr), "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]),
+                 "r"(r[6]), "r"(r[7])
+               : "memory");
+}
+// tcgen05.wait::ld binding the 8 registers of a preceding 8-register load.
+__device__ __forceinline__ void tmem_wait_ld_regs8(uint32_t (&r)[8]) {
+  asm volatile("tcgen05.wait::ld.sync.aligned;"
+               : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]), "+r"(r[6]),
+                 "+r"(r[7])
+               :
+               : "memory");
+}
+
 // tcgen05.wait::ld that also binds the 32 registers a preceding
 // tcgen05.ld wrote: every later use of them depends on the wait, so the
 // compiler cannot move a use above it (the plain wait orders only memory).
