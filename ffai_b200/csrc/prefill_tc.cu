@@ -334,8 +334,9 @@ __device__ __forceinline__ void store_row_quarter(const TcParams& p, const TcUni
 // throughout).  MUFU sustains 16 ex2 per clock per SM and the exponentials
 // of a block pair need 2048 of its cycles; the polynomial costs about ten
 // issue slots per pair on the FMA pipe.  Measured on the long-form encoder
-// workload: 0 -> 712, 1 -> 723, 2 -> 731, 3 -> 706 TFLOP/s.
-constexpr int kPolyOf8 = 2;
+// workload, 64 / 8 segments (TFLOP/s): 0 -> 794 / 762, 1 -> 798 / 766,
+// 2 -> 786 / 751, and 1 at k % 8 == 4 instead of 0 -> 778 / 754.
+constexpr int kPolyOf8 = 1;
 
 // f32 += one 16-bit half of a packed pair, in one instruction.
 template <int AB_F16>
