@@ -444,6 +444,16 @@ def bench_decode(steps: int, peaks, cpu_budget: float):
                 for c in calls:
                     c()
             r["us_plain"] = round(event_seconds(one_pass, max(5, min(steps, 50))) / layers * 1e6, 2)
+            # A decoder step knows every layer's cross-attention cache: each call
+            # also prefetches the next layer's into L2 (ffai_attn_decode_prefetch).
+            # Each layer's bytes still cross HBM once per pass, by that prefetch.
+            nxt = [caches[(i + 1) % layers] for i in range(layers)]
+            calls_pf = [lambda c=c, o=o, n=n: attention.decode(c[0], c[1], c[2], out=o,
+                                                               kv_stable=True, next_kv=(n[1], n[2]))
+                        for c, o, n in zip(caches, outs, nxt)]
+            tp = graph_seconds(calls_pf, max(5, min(steps, 50)))
+            r["prefetch_next"] = {"us": round(tp * 1e6, 2), "gbs": round(bytes_per / tp / 1e9, 1),
+                                  "frac": round(bytes_per / tp / 1e9 / peaks["hbm_gbs"], 4)}
             if cpu_budget > 0:
                 r["cpu"] = cpu_decode_rate(keys, cpu_budget)
             legs["c3_cross_1500"] = r

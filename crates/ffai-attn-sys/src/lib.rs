@@ -113,6 +113,10 @@ unsafe extern "C" {
     pub fn ffai_attn_decode(ctx: *mut ffai_attn_ctx, d: *const ffai_attn_desc, q: *const c_void,
                             k: *const c_void, v: *const c_void, o: *mut c_void, lse: *mut f32,
                             num_splits: i32, stream: *mut c_void) -> c_int;
+    pub fn ffai_attn_decode_prefetch(ctx: *mut ffai_attn_ctx, d: *const ffai_attn_desc,
+                                     q: *const c_void, k: *const c_void, v: *const c_void,
+                                     next_k: *const c_void, next_v: *const c_void,
+                                     o: *mut c_void, lse: *mut f32, stream: *mut c_void) -> c_int;
     pub fn ffai_attn_decode_static(d: *const ffai_attn_desc, q: *const c_void, k: *const c_void,
                                    v: *const c_void, o: *mut c_void, lse: *mut f32,
                                    num_splits: i32, stream: *mut c_void) -> c_int;

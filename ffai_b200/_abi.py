@@ -82,6 +82,8 @@ SIGNATURES = {
     "ffai_attn_destroy": ([_vp], None),
     "ffai_attn_prefill": ([_vp, _DescP, _vp, _vp, _vp, _vp, _vp, _vp], ctypes.c_int),
     "ffai_attn_decode": ([_vp, _DescP, _vp, _vp, _vp, _vp, _vp, _i32, _vp], ctypes.c_int),
+    "ffai_attn_decode_prefetch": ([_vp, _DescP, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp],
+                                  ctypes.c_int),
     "ffai_attn_decode_static": ([_DescP, _vp, _vp, _vp, _vp, _vp, _i32, _vp], ctypes.c_int),
     "ffai_attn_multi_prefill_host": ([ctypes.POINTER(_vp), _i32, _DescP, _vp, _vp, _vp, _vp, _vp,
                                       _i32, _i32p], ctypes.c_int),

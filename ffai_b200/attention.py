@@ -162,7 +162,7 @@ def prefill(q, k, v, *, scale: float = 1.0, q_layout="heads", k_layout="heads",
 
 def decode(q, k, v, *, scale: float = 1.0, k_layout="heads", kv_len=None, out_dtype=torch.float32,
            with_lse=False, num_splits=0, causal=False, q_offset=0, out=None, kv_stable=False,
-           kv_append_only=False):
+           kv_append_only=False, next_kv=None):
     """One decode step: q (B,H,1,64) against a K/V cache.
 
     k is (B,H,cap,64) ("heads") or (B,H,64,cap) ("kt"); v is (B,H,cap,64);
@@ -170,7 +170,9 @@ def decode(q, k, v, *, scale: float = 1.0, k_layout="heads", kv_len=None, out_dt
     queued earlier on the stream writes k/v, so the kernel may start copying
     them before the preceding kernel finishes.  `kv_append_only`: that work
     writes at most the newest key (kv_len - 1), so the others may be copied
-    early.  Returns (B,H,1,64).
+    early.  `next_kv`: (k, v) of the next decode call's cache (same shape and
+    dtype), prefetched into L2 behind this call's own reads
+    (ffai_attn_decode_prefetch; automatic split only).  Returns (B,H,1,64).
     """
     dev = _need_cuda(q, k, v)
     B, H, qlen = _dims(q, "heads")
@@ -186,8 +188,20 @@ def decode(q, k, v, *, scale: float = 1.0, k_layout="heads", kv_len=None, out_dt
                       flags=(_abi.FLAG_KV_STABLE if kv_stable else 0)
                       | (_abi.FLAG_KV_APPEND_ONLY if kv_append_only else 0))
     ctx = context(dev.index)
-    st = _abi.load().ffai_attn_decode(ctx, ctypes.byref(d), _ptr(q), _ptr(k), _ptr(v), _ptr(out),
-                                      _ptr(lse), num_splits, _stream(dev))
+    if next_kv is not None:
+        nk, nv = next_kv
+        if (nk.shape != k.shape or nv.shape != v.shape or nk.dtype != k.dtype
+                or nv.dtype != v.dtype or nk.device != k.device or nv.device != v.device
+                or not nk.is_contiguous() or not nv.is_contiguous()):
+            raise ValueError("next_kv must match k and v in shape, dtype and device, contiguous")
+        if num_splits != 0:
+            raise ValueError("next_kv needs the automatic split (num_splits=0)")
+        st = _abi.load().ffai_attn_decode_prefetch(ctx, ctypes.byref(d), _ptr(q), _ptr(k), _ptr(v),
+                                                   _ptr(nk), _ptr(nv), _ptr(out), _ptr(lse),
+                                                   _stream(dev))
+    else:
+        st = _abi.load().ffai_attn_decode(ctx, ctypes.byref(d), _ptr(q), _ptr(k), _ptr(v),
+                                          _ptr(out), _ptr(lse), num_splits, _stream(dev))
     _check(st, ctx)
     return (out, lse) if with_lse else out
 

@@ -570,7 +570,8 @@ int prefill_impl(ffai_attn_ctx* ctx, const ffai_attn_desc* d, const void* q, con
 }
 
 int decode_impl(ffai_attn_ctx* ctx, const ffai_attn_desc* d, const void* q, const void* k,
-                const void* v, void* o, float* lse, int num_splits, cudaStream_t s) {
+                const void* v, void* o, float* lse, int num_splits, cudaStream_t s,
+                const void* pf_k = nullptr, const void* pf_v = nullptr) {
   const int rows = d->batch * d->heads;
   const int cap = d->kv_capacity > 0 ? d->kv_capacity : d->kv_len;
   int kv = d->kv_len;
@@ -603,6 +604,8 @@ int decode_impl(ffai_attn_ctx* ctx, const ffai_attn_desc* d, const void* q, cons
     p.err = ctx->d_err;
     p.kv_stable = (d->flags & FFAI_ATTN_FLAG_KV_STABLE) != 0;
     p.kv_append_only = !p.kv_stable && (d->flags & FFAI_ATTN_FLAG_KV_APPEND_ONLY) != 0;
+    p.pf_k = pf_k;
+    p.pf_v = pf_v;
     FFAI_CUDA(ctx, launch_decode_cluster(p, S, kpc, s));
     return FFAI_ATTN_OK;
   }
@@ -823,6 +826,22 @@ int ffai_attn_decode(ffai_attn_ctx* ctx, const ffai_attn_desc* d, const void* q,
   DeviceGuard g(ctx->device);
   ProfScope ps(ctx, FFAI_OP_DECODE, static_cast<cudaStream_t>(stream), "ffai_attn_decode");
   return decode_impl(ctx, d, q, k, v, o, lse, num_splits, static_cast<cudaStream_t>(stream));
+}
+
+int ffai_attn_decode_prefetch(ffai_attn_ctx* ctx, const ffai_attn_desc* d, const void* q,
+                              const void* k, const void* v, const void* next_k,
+                              const void* next_v, void* o, float* lse, void* stream) {
+  if (!ctx) return set_error(nullptr, FFAI_ATTN_ERR_INVALID, "null context");
+  const int st = check_desc(ctx, d, FFAI_OP_DECODE);
+  if (st) return st;
+  if (!q || !k || !v || !o) return set_error(ctx, FFAI_ATTN_ERR_INVALID, "null operand");
+  if ((next_k == nullptr) != (next_v == nullptr))
+    return set_error(ctx, FFAI_ATTN_ERR_INVALID, "decode_prefetch: next_k and next_v go together");
+  if (reinterpret_cast<uintptr_t>(next_k) % 16 != 0 || reinterpret_cast<uintptr_t>(next_v) % 16 != 0)
+    return set_error(ctx, FFAI_ATTN_ERR_INVALID, "decode_prefetch: next cache not 16-byte aligned");
+  DeviceGuard g(ctx->device);
+  ProfScope ps(ctx, FFAI_OP_DECODE, static_cast<cudaStream_t>(stream), "ffai_attn_decode_prefetch");
+  return decode_impl(ctx, d, q, k, v, o, lse, 0, static_cast<cudaStream_t>(stream), next_k, next_v);
 }
 
 int ffai_attn_varlen(ffai_attn_ctx* ctx, const ffai_attn_desc* d, const int32_t* cu_q,
@@ -1148,7 +1167,7 @@ int ffai_attn_decode_paged(ffai_attn_ctx* ctx, const ffai_attn_desc* d, const vo
                            const void* k_pool, const void* v_pool, int32_t num_pages,
                            const int32_t* block_table, const int32_t* seq_lens, int32_t max_pages,
                            void* o, float* lse, void* stream) {
-  DecodeParams p;
+  DecodeParams p{};
   int st = paged_params(ctx, d, k_pool, v_pool, num_pages, block_table, seq_lens, max_pages, p);
   if (st) return st;
   if (d->q_len != 1) return set_error(ctx, FFAI_ATTN_DECLINED, "decode: q_len must be 1");
@@ -1179,7 +1198,7 @@ int ffai_attn_decode_paged(ffai_attn_ctx* ctx, const ffai_attn_desc* d, const vo
 int ffai_kv_append(ffai_attn_ctx* ctx, const ffai_attn_desc* d, void* k_pool, void* v_pool,
                    int32_t num_pages, const int32_t* block_table, int32_t* seq_lens,
                    int32_t max_pages, const void* k_new, const void* v_new, void* stream) {
-  DecodeParams p;
+  DecodeParams p{};
   int st = paged_params(ctx, d, k_pool, v_pool, num_pages, block_table, seq_lens, max_pages, p);
   if (st) return st;
   if (!k_new || !v_new) return set_error(ctx, FFAI_ATTN_ERR_INVALID, "null key or value");
@@ -1191,7 +1210,7 @@ int ffai_kv_append(ffai_attn_ctx* ctx, const ffai_attn_desc* d, void* k_pool, vo
 int ffai_kv_copy_pages(ffai_attn_ctx* ctx, const ffai_attn_desc* d, void* k_pool, void* v_pool,
                        int32_t num_pages, const int32_t* src_pages, const int32_t* dst_pages,
                        int32_t n, void* stream) {
-  DecodeParams p;
+  DecodeParams p{};
   static const int32_t kOne = 0;
   int st = paged_params(ctx, d, k_pool, v_pool, num_pages, &kOne, &kOne, 1, p);
   if (st) return st;

@@ -196,6 +196,14 @@ __device__ __forceinline__ void bulk_load(void* smem_dst, const void* gsrc, uint
       : "memory");
 }
 
+// Bring `bytes` (a multiple of 16, 16-byte aligned) of global memory into L2,
+// fire and forget: no shared memory, no barrier.
+__device__ __forceinline__ void bulk_prefetch_l2(const void* gsrc, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(reinterpret_cast<uint64_t>(gsrc)),
+               "r"(bytes)
+               : "memory");
+}
+
 // 3-d tiled TMA store of one box from shared memory (bulk async-group of
 // the issuing thread).  The box starts at a non-negative, 16-byte aligned x.
 __device__ __forceinline__ void tma_store_3d(const CUtensorMap* map, const void* smem_src, int c0,

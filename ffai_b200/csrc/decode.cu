@@ -413,6 +413,13 @@ __global__ void __launch_bounds__(kClThreads, 2) decode_cluster_kernel(DecodePar
           mbar_arrive(&full[st]);
         }
         ++issued;
+        // The ring is filled (or the range issued): bring the same keys of
+        // the next call's cache into L2 behind this CTA's own copies.
+        if (!PAGED && p.pf_k && c == min(nch, kClStages) - 1) {
+          const uint32_t pf = static_cast<uint32_t>(k1 - k0) * 64 * sizeof(T);
+          bulk_prefetch_l2(static_cast<const T*>(p.pf_k) + base, pf);
+          bulk_prefetch_l2(static_cast<const T*>(p.pf_v) + base, pf);
+        }
       }
       if (s_abort) {
         // Wait (bounded, ignoring the abort flag) for the last armed phase of

@@ -42,6 +42,11 @@ struct DecodeParams {
   int kv_stable;  // cluster kernel: copy K/V before the programmatic-dependency wait
   int kv_append_only;  // cluster kernel: only key kv_len - 1 may be written by the
                        // preceding kernel; copy the others before the wait
+  // cluster kernel, row-major caches: another cache of the same shape (the next
+  // decode call's) whose keys [k0, k1) of each CTA's row are prefetched into L2
+  // once the CTA's own copies are issued; null for none
+  const void* pf_k;
+  const void* pf_v;
   // paged caches (launch_decode_paged): k, v are pools of pages of kPageKeys
   // keys, (num_pages, heads, kPageKeys, 64); row = b * heads + h
   const int* block_table;  // (batch, max_pages) page ids

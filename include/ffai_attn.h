@@ -170,6 +170,23 @@ int ffai_attn_prefill(ffai_attn_ctx* ctx, const ffai_attn_desc* d, const void* q
 int ffai_attn_decode(ffai_attn_ctx* ctx, const ffai_attn_desc* d, const void* q, const void* k,
                      const void* v, void* o, float* lse, int32_t num_splits, void* stream);
 
+/* ffai_attn_decode (automatic split) that also brings another cache of the
+ * same shape, dtype and layout -- the next decode call's, e.g. the next
+ * layer's cross-attention keys and values, which a decoder step knows in
+ * advance -- into L2 while this call streams its own: each CTA of the cluster
+ * kernel prefetches (cp.async.bulk.prefetch.L2) the same key range of the
+ * same row of next_k / next_v once its own copies are issued, so the next
+ * call reads them from L2 and HBM keeps streaming through this call's tail.
+ * A prefetch only fills the cache, it reads nothing into this call's results,
+ * so next_k / next_v may still be written by other work.  Results are those
+ * of ffai_attn_decode with num_splits 0.  Both null: no prefetch.  Only the
+ * cluster kernel (row-major caches with batch x heads x 8 >= the GPU's SMs)
+ * prefetches; other shapes ignore the hint.  No reference counterpart (the
+ * reference's decode heads read host memory, flash_attn.rs:602-789). */
+int ffai_attn_decode_prefetch(ffai_attn_ctx* ctx, const ffai_attn_desc* d, const void* q,
+                              const void* k, const void* v, const void* next_k,
+                              const void* next_v, void* o, float* lse, void* stream);
+
 /* Decode as ffai_attn_decode's split kernel does (same chunking for the same
  * num_splits, same results), but with no context and no memory allocation:
  * it calls no cudaMalloc / cudaFree or allocating library function.  For

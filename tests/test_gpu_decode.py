@@ -186,3 +186,57 @@ def test_decode_kv_append_only_sees_the_appended_key(oracle):
     for step, (o, (kr, vr)) in enumerate(zip(outs, refs)):
         ref = _oracle_decode(oracle, q, kr, vr)
         assert_f32_close(f32np(o), ref, f"append step {step}")
+
+
+# ------------------------------------------------ next-call L2 prefetch (ffai_attn_decode_prefetch)
+@pytest.mark.parametrize("keys,beams,heads,dtype", [
+    (1500, 5, 12, torch.bfloat16), (448, 5, 12, torch.bfloat16), (1500, 5, 12, torch.float16),
+    (300, 5, 12, torch.float32), (37, 5, 12, torch.bfloat16), (1500, 1, 2, torch.bfloat16)])
+def test_decode_prefetch_same_bits(keys, beams, heads, dtype):
+    """Prefetching the next call's cache into L2 reads nothing into this call:
+    the results are ffai_attn_decode's bit for bit, on the cluster kernel's
+    shapes and on one (2 rows) where the hint is ignored."""
+    q, k, v = workloads.decode_inputs(keys, seed=31, dtype=dtype, beams=beams, heads=heads)
+    _, nk, nv = workloads.decode_inputs(keys, seed=32, dtype=dtype, beams=beams, heads=heads)
+    qd, kd, vd = q.to(DEV), k.to(DEV), v.to(DEV)
+    nkd, nvd = nk.to(DEV), nv.to(DEV)
+    a, la = attention.decode(qd, kd, vd, with_lse=True)
+    a, la = a.clone(), la.clone()
+    b, lb = attention.decode(qd, kd, vd, with_lse=True, next_kv=(nkd, nvd), kv_stable=True)
+    assert torch.equal(a, b) and torch.equal(la, lb)
+
+
+def test_decode_prefetch_chain_of_layers(oracle):
+    """A step over several layers' caches, each call prefetching the next
+    layer's (the last one the first's): every output matches the oracle."""
+    layers = 4
+    caches = [workloads.decode_inputs(1500, seed=40 + i) for i in range(layers)]
+    dev = [(q.to(DEV), k.to(DEV), v.to(DEV)) for q, k, v in caches]
+    outs = []
+    for i, (q, k, v) in enumerate(dev):
+        _, nk, nv = dev[(i + 1) % layers]
+        outs.append(attention.decode(q, k, v, next_kv=(nk, nv), kv_stable=True))
+    torch.cuda.synchronize()
+    for (q, k, v), o in zip(caches, outs):
+        assert_f32_close(f32np(o), _oracle_decode(oracle, q, k, v), "prefetch chain")
+
+
+def test_decode_prefetch_arguments():
+    import ctypes
+    from ffai_b200 import _abi
+    q, k, v = workloads.decode_inputs(1500, seed=33)
+    qd, kd, vd = q.to(DEV), k.to(DEV), v.to(DEV)
+    with pytest.raises(ValueError):  # next cache of another shape
+        attention.decode(qd, kd, vd, next_kv=(kd[:, :, :100].contiguous(), vd[:, :, :100].contiguous()))
+    with pytest.raises(ValueError):  # explicit split counts do not prefetch
+        attention.decode(qd, kd, vd, next_kv=(kd, vd), num_splits=4)
+    # one of the two pointers alone is an error from the library
+    out = torch.empty(5, 12, 1, 64, device=DEV)
+    d = _abi.new_desc(batch=5, heads=12, q_len=1, kv_len=1500, kv_capacity=1500,
+                      q_dtype=attention._DT[qd.dtype], kv_dtype=attention._DT[kd.dtype],
+                      out_dtype=attention._DT[out.dtype], scale=1.0)
+    ctx = attention.context(0)
+    st = _abi.load().ffai_attn_decode_prefetch(ctx, ctypes.byref(d), qd.data_ptr(), kd.data_ptr(),
+                                               vd.data_ptr(), kd.data_ptr(), None,
+                                               out.data_ptr(), None, None)
+    assert st == _abi.ERR_INVALID
