@@ -523,31 +523,33 @@ int prefill_impl(ffai_attn_ctx* ctx, const ffai_attn_desc* d, const void* q, con
     int st = ensure(ctx, reinterpret_cast<uint16_t**>(&ctx->d_stage), &ctx->stage_cap, stage);
     if (st) return st;
     uint16_t* base = static_cast<uint16_t*>(ctx->d_stage);
+    // One launch converts every staged operand.
+    StageBatch sb{};
+    sb.B = B;
+    sb.H = H;
     if (stage_q) {
-      FFAI_CUDA(ctx, launch_to_16bit_heads_split(q, d->q_dtype,
-                                                 strides_of(d->q_layout, H, Nq, d->token_stride), B,
-                                                 H, Nq, base, dt16 == FFAI_DT_F16, s));
+      sb.op[sb.n++] = StageOp{q, d->q_dtype, strides_of(d->q_layout, H, Nq, d->token_stride), Nq,
+                              base, 0, 0};
       qq = base;
       q_tm = false;
       base += q_elems;
     }
     if (stage_k) {
-      FFAI_CUDA(ctx, launch_to_16bit_heads_split(k, d->kv_dtype,
-                                                 strides_of(d->k_layout, H, cap, d->token_stride), B,
-                                                 H, Nk, base, dt16 == FFAI_DT_F16, s));
+      sb.op[sb.n++] = StageOp{k, d->kv_dtype, strides_of(d->k_layout, H, cap, d->token_stride), Nk,
+                              base, 0, 0};
       kk = base;
       k_tm = false;
       kcap = Nk;
       base += kv_elems;
     }
     if (stage_v) {
-      FFAI_CUDA(ctx, launch_to_16bit_heads_split(v, d->kv_dtype,
-                                                 strides_of(d->v_layout, H, cap, d->token_stride), B,
-                                                 H, Nk, base, dt16 == FFAI_DT_F16, s));
+      sb.op[sb.n++] = StageOp{v, d->kv_dtype, strides_of(d->v_layout, H, cap, d->token_stride), Nk,
+                              base, 0, 0};
       vv = base;
       v_tm = false;
       vcap = Nk;
     }
+    FFAI_CUDA(ctx, launch_stage_batch(sb, dt16 == FFAI_DT_F16, s));
   }
   const int ab_f16 = dt16 == FFAI_DT_F16;
 

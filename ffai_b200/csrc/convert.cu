@@ -1,8 +1,9 @@
-// Operand preparation for the tensor-core prefill: gather an f32/bf16/f16
-// operand of any supported layout into a contiguous heads-split (B,H,N,64)
-// 16-bit (bf16 or f16) buffer.  Used for the reference's f32 operands (its callers hold f32
-// candle tensors, flash_attn.rs:212-217) and for K^T (B,H,64,N) whose row
-// pitch is not a multiple of 16 bytes and so cannot be described to TMA.
+// Operand preparation for the tensor-core prefill: gather f32/bf16/f16
+// operands of any supported layout into contiguous heads-split (B,H,N,64)
+// 16-bit (bf16 or f16) buffers, all of a call's operands in one launch.
+// Used for the reference's f32 operands (its callers hold f32 candle tensors,
+// flash_attn.rs:212-217) and for K^T (B,H,64,N) whose row pitch is not a
+// multiple of 16 bytes and so cannot be described to TMA.
 #include "common.cuh"
 #include "kernels.h"
 
@@ -15,88 +16,106 @@ __device__ __forceinline__ uint32_t pack16(float lo, float hi) {
   return F16 ? pack_f16x2(lo, hi) : pack_bf16x2(lo, hi);
 }
 
+// Row-major source: one warp per destination row (64 elements, two per lane).
 template <typename T, bool F16>
-__global__ void to_16bit_rows_kernel(const T* __restrict__ src, Strides st, int H, int N,
-                                     uint16_t* __restrict__ dst, long long total_rows) {
-  // One warp per destination row (64 elements, two per lane).
-  const long long row = (static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x) / 32;
+__device__ __forceinline__ void stage_rows(const StageOp& op, int H, long long blk) {
+  const long long rows = op.rows;
+  const long long row = (blk * 256 + threadIdx.x) / 32;
   const int lane = threadIdx.x % 32;
-  if (row >= total_rows) return;
-  const int n = static_cast<int>(row % N);
-  const long long bh = row / N;
+  if (row >= rows) return;
+  const Strides st = op.st;
+  const int n = static_cast<int>(row % op.N);
+  const long long bh = row / op.N;
   const int h = static_cast<int>(bh % H);
   const long long b = bh / H;
-  const T* s = src + b * st.sb + h * st.sh + n * st.sr;
+  const T* s = static_cast<const T*>(op.src) + b * st.sb + h * st.sh + n * st.sr;
   const float x0 = to_f32(s[(2 * lane) * st.sd]);
   const float x1 = to_f32(s[(2 * lane + 1) * st.sd]);
-  reinterpret_cast<uint32_t*>(dst + row * 64)[lane] = pack16<F16>(x0, x1);
+  reinterpret_cast<uint32_t*>(op.dst + row * 64)[lane] = pack16<F16>(x0, x1);
 }
 
-// Head-dim-major source (sd != 1, sr == 1): transpose 64x64 tiles through
+// Head-dim-major source (sd != 1, sr == 1): a 64x64 tile transposed through
 // shared memory so both the reads (along keys) and writes (along dims) coalesce.
 template <typename T, bool F16>
-__global__ void kt_to_16bit_rows_kernel(const T* __restrict__ src, Strides st, int H, int N,
-                                        uint16_t* __restrict__ dst) {
-  __shared__ float tile[64][65];
-  const int bh = blockIdx.y;
-  const int h = bh % H;
+__device__ __forceinline__ void stage_kt(const StageOp& op, int H, long long blk,
+                                         float (&tile)[64][65]) {
+  const int ntiles = (op.N + 63) / 64;
+  const long long bh = blk / ntiles;
+  const int n0 = static_cast<int>(blk % ntiles) * 64;
+  const int h = static_cast<int>(bh % H);
   const long long b = bh / H;
-  const int n0 = blockIdx.x * 64;
-  const T* s = src + b * st.sb + h * st.sh;
+  const Strides st = op.st;
+  const T* s = static_cast<const T*>(op.src) + b * st.sb + h * st.sh;
   for (int idx = threadIdx.x; idx < 64 * 64; idx += blockDim.x) {
     const int d = idx / 64, j = idx % 64;
     const int n = n0 + j;
-    tile[d][j] = n < N ? to_f32(s[static_cast<long long>(n) * st.sr + d * st.sd]) : 0.f;
+    tile[d][j] = n < op.N ? to_f32(s[static_cast<long long>(n) * st.sr + d * st.sd]) : 0.f;
   }
   __syncthreads();
-  uint16_t* o = dst + (static_cast<long long>(bh) * N) * 64;
+  uint16_t* o = op.dst + (bh * op.N) * 64;
   for (int idx = threadIdx.x; idx < 64 * 32; idx += blockDim.x) {
     const int j = idx / 32, dp = idx % 32;
     const int n = n0 + j;
-    if (n < N)
+    if (n < op.N)
       reinterpret_cast<uint32_t*>(o + static_cast<long long>(n) * 64)[dp] =
           pack16<F16>(tile[2 * dp][j], tile[2 * dp + 1][j]);
   }
 }
 
-template <typename T, bool F16>
-cudaError_t launch_typed(const void* src, Strides st, int B, int H, int N, void* dst,
-                         cudaStream_t s) {
-  const T* sp = static_cast<const T*>(src);
-  uint16_t* dp = static_cast<uint16_t*>(dst);
-  if (st.sd != 1 && st.sr == 1) {
-    dim3 grid((N + 63) / 64, B * H);
-    kt_to_16bit_rows_kernel<T, F16><<<grid, 256, 0, s>>>(sp, st, H, N, dp);
-  } else {
-    const long long rows = static_cast<long long>(B) * H * N;
-    const long long blocks = (rows * 32 + 255) / 256;
-    to_16bit_rows_kernel<T, F16><<<static_cast<unsigned>(blocks), 256, 0, s>>>(sp, st, H, N, dp,
-                                                                              rows);
-  }
-  return cudaGetLastError();
-}
-
+// Up to three operands in one launch (q, k, v of one prefill call): block
+// ranges [end[i-1], end[i]) convert operand i, with the row-major or the
+// K^T body above.  A programmatic dependent of the preceding kernel (its
+// sources may come from there), letting the prefill that reads its output
+// launch at once.
 template <bool F16>
-cudaError_t launch_dst(const void* src, int src_dtype, Strides st, int B, int H, int N, void* dst,
-                       cudaStream_t s) {
-  switch (src_dtype) {
-    case 0:
-      return launch_typed<float, F16>(src, st, B, H, N, dst, s);
-    case 1:
-      return launch_typed<__nv_bfloat16, F16>(src, st, B, H, N, dst, s);
-    case 2:
-      return launch_typed<__half, F16>(src, st, B, H, N, dst, s);
+__global__ void __launch_bounds__(256) stage_kernel(StageBatch sb) {
+  __shared__ float tile[64][65];
+  griddep_wait();
+  griddep_launch_dependents();
+  int i = 0;
+  while (i + 1 < sb.n && blockIdx.x >= sb.end[i]) ++i;
+  const StageOp& op = sb.op[i];
+  const long long blk = static_cast<long long>(blockIdx.x) - (i ? sb.end[i - 1] : 0);
+  if (op.kt) {
+    switch (op.src_dtype) {
+      case 0: stage_kt<float, F16>(op, sb.H, blk, tile); break;
+      case 1: stage_kt<__nv_bfloat16, F16>(op, sb.H, blk, tile); break;
+      default: stage_kt<__half, F16>(op, sb.H, blk, tile); break;
+    }
+  } else {
+    switch (op.src_dtype) {
+      case 0: stage_rows<float, F16>(op, sb.H, blk); break;
+      case 1: stage_rows<__nv_bfloat16, F16>(op, sb.H, blk); break;
+      default: stage_rows<__half, F16>(op, sb.H, blk); break;
+    }
   }
-  return cudaErrorInvalidValue;
 }
 
 }  // namespace
 
-cudaError_t launch_to_16bit_heads_split(const void* src, int src_dtype, Strides st, int B, int H,
-                                        int N, void* dst, int dst_f16, cudaStream_t s) {
-  if (B <= 0 || H <= 0 || N <= 0) return cudaSuccess;
-  return dst_f16 ? launch_dst<true>(src, src_dtype, st, B, H, N, dst, s)
-                 : launch_dst<false>(src, src_dtype, st, B, H, N, dst, s);
+cudaError_t launch_stage_batch(StageBatch sb, int dst_f16, cudaStream_t s) {
+  long long blocks = 0;
+  for (int i = 0; i < sb.n; ++i) {
+    StageOp& op = sb.op[i];
+    if (op.src_dtype < 0 || op.src_dtype > 2) return cudaErrorInvalidValue;
+    op.kt = op.st.sd != 1 && op.st.sr == 1;
+    op.rows = static_cast<long long>(sb.B) * sb.H * op.N;
+    blocks += op.kt ? static_cast<long long>((op.N + 63) / 64) * sb.B * sb.H : (op.rows * 32 + 255) / 256;
+    sb.end[i] = blocks;
+  }
+  if (sb.n <= 0 || blocks <= 0) return cudaSuccess;
+  if (blocks > 0x7fffffffLL) return cudaErrorInvalidValue;
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3(static_cast<unsigned>(blocks));
+  cfg.blockDim = dim3(256);
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return dst_f16 ? cudaLaunchKernelEx(&cfg, stage_kernel<true>, sb)
+                 : cudaLaunchKernelEx(&cfg, stage_kernel<false>, sb);
 }
 
 }  // namespace ffai

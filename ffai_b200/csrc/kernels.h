@@ -302,7 +302,24 @@ size_t prefill_tc_smem_bytes();
 // dst (B,H,N,64) heads-split contiguous 16-bit (bf16, or f16 when dst_f16)
 // <- src element (b,h,row,d) at b*sb + h*sh + row*sr + d*sd of f32 / bf16 /
 // f16 (src_dtype 0/1/2).
-cudaError_t launch_to_16bit_heads_split(const void* src, int src_dtype, Strides st, int B, int H,
-                                        int N, void* dst, int dst_f16, cudaStream_t s);
+// Several operands of one call (B, H shared) converted in one launch, each
+// into its own contiguous heads-split 16-bit buffer of B*H*N rows; the launch
+// is a programmatic dependent of the preceding kernel.
+struct StageOp {
+  const void* src;
+  int src_dtype;
+  Strides st;
+  int N;
+  uint16_t* dst;
+  int kt;          // set by the launcher: head-dim-major source
+  long long rows;  // set by the launcher
+};
+struct StageBatch {
+  StageOp op[3];
+  int n;
+  int B, H;
+  long long end[3];  // set by the launcher: cumulative block counts
+};
+cudaError_t launch_stage_batch(StageBatch sb, int dst_f16, cudaStream_t s);
 
 }  // namespace ffai
