@@ -11,7 +11,7 @@
 // query rows (two 128-row tiles, t = 0, 1) of one (sequence, head); both
 // tiles share every K/V block, so each block is fetched once for 256 rows.
 //
-//   warp 16     TMA producer: Q tiles, then a 3-stage ring of K/V blocks of
+//   warp 16     TMA producer: Q tiles, then a 4-stage ring of K/V blocks of
 //               128 keys (16 KB each, 128-byte swizzle).  Also owns TMEM.
 //   warps 17,18 MMA issuers, one warp per tile:   S_t = Q_t K^T   (M=128, N=128, K=64)
 //                                         O_t += P_t V    (M=128, N=64,  K=128)
